@@ -1,0 +1,201 @@
+// Memory-bound kernels of the forward pass: embedding gather + LayerNorm,
+// residual LayerNorm, masked mean-pool + L2 normalise, f32 -> f16.
+//
+// Row kernels use one warp per 768-wide row: 24 floats per lane in float4s,
+// warp-shuffle reductions, no shared memory.
+#include "common.cuh"
+#include "gguf_decode.cuh"
+#include "kernels.h"
+
+namespace le {
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+__device__ __forceinline__ double warp_sum_d(double v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+// ops_simd.go:7-24: mean = sum/n, var = sumSq/n - mean^2 (single pass, f32),
+// invStd = float32(1 / sqrt(float64(var + eps))), y = (x-mean)*invStd*w + b.
+// H is a multiple of 128 and at most 128 * LN_MAXV.
+constexpr int LN_MAXV = 8;  // float4 per lane -> H <= 1024
+
+template <bool GATHER>
+__global__ void __launch_bounds__(256) ln_rows_kernel(const float* in, const int32_t* __restrict__ ids,
+                                                      int emb_type, const uint8_t* __restrict__ emb, long emb_row_bytes,
+                                                      const float* __restrict__ type0, const float* __restrict__ w,
+                                                      const float* __restrict__ b, float eps, int T, int H,
+                                                      int vocab, DevStatus* status, float* out32,
+                                                      __half* __restrict__ out16) {
+  const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (warp >= T) return;
+  const int nv = H / 128;
+  float4 x[LN_MAXV];
+  if constexpr (GATHER) {
+    // bert.go:227-247: token_embd row + token_types row 0, then LayerNorm.
+    int id = ids[warp];
+    if (id < 0 || id >= vocab) {  // device-resident ids are not checked on the host
+      if (lane == 0) report(status, DE_BOUNDS, 1, id);
+      id = 0;
+    }
+    const uint8_t* row = emb + (long)id * emb_row_bytes;
+#pragma unroll
+    for (int i = 0; i < LN_MAXV; i++) {
+      if (i < nv) {
+        const int c = (i * 32 + lane) * 4;
+        const float4 t = *reinterpret_cast<const float4*>(type0 + c);
+        x[i].x = __fadd_rn(gguf_elem(emb_type, row, c + 0), t.x);
+        x[i].y = __fadd_rn(gguf_elem(emb_type, row, c + 1), t.y);
+        x[i].z = __fadd_rn(gguf_elem(emb_type, row, c + 2), t.z);
+        x[i].w = __fadd_rn(gguf_elem(emb_type, row, c + 3), t.w);
+      }
+    }
+  } else {
+    const float* r = in + (long)warp * H;
+#pragma unroll
+    for (int i = 0; i < LN_MAXV; i++)
+      if (i < nv) x[i] = *reinterpret_cast<const float4*>(r + (i * 32 + lane) * 4);
+  }
+  float s = 0.f, ss = 0.f;
+#pragma unroll
+  for (int i = 0; i < LN_MAXV; i++)
+    if (i < nv) {
+      s += x[i].x + x[i].y + x[i].z + x[i].w;
+      ss += x[i].x * x[i].x + x[i].y * x[i].y + x[i].z * x[i].z + x[i].w * x[i].w;
+    }
+  s = warp_sum(s);
+  ss = warp_sum(ss);
+  const float nf = (float)H;
+  const float mean = __fdiv_rn(s, nf);
+  const float var = __fsub_rn(__fdiv_rn(ss, nf), __fmul_rn(mean, mean));
+  const float inv = (float)(1.0 / sqrt((double)__fadd_rn(var, eps)));
+  float* o32 = out32 + (long)warp * H;
+  __half* o16 = out16 + (long)warp * H;
+#pragma unroll
+  for (int i = 0; i < LN_MAXV; i++)
+    if (i < nv) {
+      const int c = (i * 32 + lane) * 4;
+      const float4 ww = *reinterpret_cast<const float4*>(w + c);
+      const float4 bb = *reinterpret_cast<const float4*>(b + c);
+      float4 y;
+      y.x = __fadd_rn(__fmul_rn(__fmul_rn(__fsub_rn(x[i].x, mean), inv), ww.x), bb.x);
+      y.y = __fadd_rn(__fmul_rn(__fmul_rn(__fsub_rn(x[i].y, mean), inv), ww.y), bb.y);
+      y.z = __fadd_rn(__fmul_rn(__fmul_rn(__fsub_rn(x[i].z, mean), inv), ww.z), bb.z);
+      y.w = __fadd_rn(__fmul_rn(__fmul_rn(__fsub_rn(x[i].w, mean), inv), ww.w), bb.w);
+      *reinterpret_cast<float4*>(o32 + c) = y;
+      uint2 h;
+      h.x = pack_half2(y.x, y.y);
+      h.y = pack_half2(y.z, y.w);
+      *reinterpret_cast<uint2*>(o16 + c) = h;
+    }
+}
+
+// pool.go:8-53 + embedder.go:59-68: masked mean (f32 sum, x (1/count)),
+// L2 normalise (float64 sum of squares, float32 multiply by float32(1/norm)),
+// then Matryoshka truncation to out_dim and renormalisation.  One CTA of
+// H/4 threads per sequence; empty sequences give a zero vector.
+__global__ void pool_kernel(const float* __restrict__ h, const int32_t* __restrict__ offsets, int H, int out_dim,
+                            float* __restrict__ out) {
+  const int s = blockIdx.x;
+  const int t0 = offsets[s], t1 = offsets[s + 1];
+  const int c = threadIdx.x * 4;
+  __shared__ double red[32];
+  float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+  if (c < H) {
+    for (int t = t0; t < t1; t++) {
+      const float4 v = *reinterpret_cast<const float4*>(h + (long)t * H + c);
+      acc.x += v.x;
+      acc.y += v.y;
+      acc.z += v.z;
+      acc.w += v.w;
+    }
+    if (t1 > t0) {
+      const float inv = __fdiv_rn(1.0f, (float)(t1 - t0));
+      acc.x = __fmul_rn(acc.x, inv);
+      acc.y = __fmul_rn(acc.y, inv);
+      acc.z = __fmul_rn(acc.z, inv);
+      acc.w = __fmul_rn(acc.w, inv);
+    }
+  }
+  float v[4] = {acc.x, acc.y, acc.z, acc.w};
+  for (int pass = 0; pass < 2; pass++) {
+    const int lim = pass == 0 ? H : out_dim;
+    if (pass == 1 && out_dim >= H) break;
+    double sq = 0.0;
+    for (int i = 0; i < 4; i++)
+      if (c + i < lim) sq += (double)v[i] * (double)v[i];
+    sq = warp_sum_d(sq);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = (blockDim.x + 31) >> 5;
+    __syncthreads();
+    if (lane == 0) red[warp] = sq;
+    __syncthreads();
+    double tot = 0.0;
+    for (int i = 0; i < nw; i++) tot += red[i];
+    const double norm = sqrt(tot);
+    if (norm != 0.0) {
+      const float inv = (float)(1.0 / norm);
+      for (int i = 0; i < 4; i++) v[i] = __fmul_rn(v[i], inv);
+    }
+  }
+  for (int i = 0; i < 4; i++)
+    if (c + i < out_dim) out[(long)s * out_dim + c + i] = v[i];
+}
+
+__global__ void f32_to_f16_kernel(const float* __restrict__ in, long n, __half* __restrict__ out) {
+  const long i = (long)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < n) out[i] = __float2half_rn(in[i]);
+}
+
+// Per-token position inside its sequence (RoPE row index, bert.go:351).
+__global__ void positions_kernel(const int32_t* __restrict__ offsets, int nseq, int32_t* __restrict__ pos) {
+  const int s = blockIdx.x;
+  if (s >= nseq) return;
+  const int t0 = offsets[s], t1 = offsets[s + 1];
+  for (int t = t0 + threadIdx.x; t < t1; t += blockDim.x) pos[t] = t - t0;
+}
+
+cudaError_t launch_embed_ln(const int32_t* ids, int emb_type, const uint8_t* emb, long emb_row_bytes, int vocab,
+                            const float* type0, const float* w, const float* b, float eps, int T, int H, float* out32,
+                            __half* out16, DevStatus* status, cudaStream_t s) {
+  if (H % 128 || H > 128 * LN_MAXV) return cudaErrorInvalidValue;
+  if (T == 0) return cudaSuccess;
+  ln_rows_kernel<true><<<(T + 7) / 8, 256, 0, s>>>(nullptr, ids, emb_type, emb, emb_row_bytes, type0, w, b, eps, T, H,
+                                                   vocab, status, out32, out16);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_ln(const float* in, const float* w, const float* b, float eps, int T, int H, float* out32,
+                      __half* out16, cudaStream_t s) {
+  if (H % 128 || H > 128 * LN_MAXV) return cudaErrorInvalidValue;
+  if (T == 0) return cudaSuccess;
+  ln_rows_kernel<false><<<(T + 7) / 8, 256, 0, s>>>(in, nullptr, 0, nullptr, 0, nullptr, w, b, eps, T, H, 0, nullptr,
+                                                    out32, out16);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_pool(const float* h, const int32_t* offsets, int nseq, int H, int out_dim, float* out,
+                        cudaStream_t s) {
+  if (nseq == 0) return cudaSuccess;
+  pool_kernel<<<nseq, H / 4, 0, s>>>(h, offsets, H, out_dim, out);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_f32_to_f16(const float* in, long n, __half* out, cudaStream_t s) {
+  if (n == 0) return cudaSuccess;
+  f32_to_f16_kernel<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(in, n, out);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_positions(const int32_t* offsets, int nseq, int32_t* pos, cudaStream_t s) {
+  if (nseq == 0) return cudaSuccess;
+  positions_kernel<<<nseq, 128, 0, s>>>(offsets, nseq, pos);
+  return cudaGetLastError();
+}
+
+}  // namespace le

@@ -1,0 +1,92 @@
+// GEMM epilogues shared by every GEMM kernel.  They receive output values in
+// pairs (va, vb) of the GEMM's "virtual" output rows a, b:
+//   EPI_F32    plain float32 store (standalone qgemm op)
+//   EPI_QKV    QKV projection: RoPE on the Q and K columns (adjacent pairs
+//              2i, 2i+1 of each head, ops_simd.go:127-137), fp16 store
+//   EPI_RESID  h += acc (bert.go:262-265, 276-279), float32 store
+//   EPI_GEGLU  merged up/gate: gelu(gate) * up (bert.go:431-436), fp16 store
+#pragma once
+#include "common.cuh"
+
+namespace le {
+
+enum EpiMode : int { EPI_F32 = 0, EPI_QKV = 1, EPI_RESID = 2, EPI_GEGLU = 3 };
+
+struct EpiParams {
+  int mode;
+  int M;           // valid output rows (tokens)
+  int N;           // output columns of the real result
+  float* out32;    // EPI_F32, EPI_RESID
+  __half* out16;   // EPI_QKV, EPI_GEGLU
+  long ldo;        // leading dimension of out (elements)
+  const float* resid;  // EPI_RESID (may alias out32)
+  const int32_t* pos;  // EPI_QKV: position of each token in its sequence
+  const float* rope_cos;  // [max_pos][head_dim/2]
+  const float* rope_sin;
+  int head_dim;
+  int rope_cols;   // columns [0, rope_cols) get RoPE (= 2 * hidden)
+};
+
+// ops_simd.go:27-43, same operation order.
+__device__ __forceinline__ float gelu_ref(float v) {
+  const float t = __fmul_rn(__fmul_rn(0.7978845608f, v), __fadd_rn(1.0f, __fmul_rn(__fmul_rn(0.044715f, v), v)));
+  const float t2 = __fmul_rn(t, t);
+  float th = __fdiv_rn(__fmul_rn(t, __fadd_rn(27.0f, t2)), __fadd_rn(27.0f, __fmul_rn(9.0f, t2)));
+  if (t > 4.97f) th = 1.0f;
+  else if (t < -4.97f) th = -1.0f;
+  return __fmul_rn(__fmul_rn(0.5f, v), __fadd_rn(1.0f, th));
+}
+
+// Map GEMM output pair index p to virtual rows (a, b) and output columns.
+// EPI_GEGLU: tile t = p/128 holds up rows t*256 + c and gate rows
+// t*256 + 128 + c for output column t*128 + c.  Others: a = 2p, b = 2p+1.
+__device__ __forceinline__ void pair_rows(int mode, int p, int* a, int* b) {
+  if (mode == EPI_GEGLU) {
+    const int t = p >> 7, c = p & 127;
+    *a = t * 256 + c;
+    *b = *a + 128;
+  } else {
+    *a = 2 * p;
+    *b = 2 * p + 1;
+  }
+}
+
+// Apply the epilogue to one pair.  For EPI_GEGLU, `a` is the up row (its
+// output column is t*128 + c) and va/vb are (up, gate).
+__device__ __forceinline__ void epi_pair(const EpiParams& ep, int m, int a, float va, float vb) {
+  switch (ep.mode) {
+    case EPI_F32: {
+      float* o = ep.out32 + (long)m * ep.ldo;
+      if (a < ep.N) o[a] = va;
+      if (a + 1 < ep.N) o[a + 1] = vb;
+      break;
+    }
+    case EPI_QKV: {
+      if (a >= ep.N) return;
+      float x0 = va, x1 = vb;
+      if (a < ep.rope_cols) {
+        const int i = (a % ep.head_dim) >> 1;
+        const long r = (long)ep.pos[m] * (ep.head_dim >> 1) + i;
+        const float c = ep.rope_cos[r], s = ep.rope_sin[r];
+        x0 = __fsub_rn(__fmul_rn(va, c), __fmul_rn(vb, s));
+        x1 = __fadd_rn(__fmul_rn(va, s), __fmul_rn(vb, c));
+      }
+      *reinterpret_cast<uint32_t*>(ep.out16 + (long)m * ep.ldo + a) = pack_half2(x0, x1);
+      break;
+    }
+    case EPI_RESID: {
+      if (a >= ep.N) return;
+      const float2 r = *reinterpret_cast<const float2*>(ep.resid + (long)m * ep.ldo + a);
+      *reinterpret_cast<float2*>(ep.out32 + (long)m * ep.ldo + a) = make_float2(__fadd_rn(r.x, va), __fadd_rn(r.y, vb));
+      break;
+    }
+    case EPI_GEGLU: {
+      const int col = (a >> 8) * 128 + (a & 127);
+      if (col >= ep.N) return;
+      ep.out16[(long)m * ep.ldo + col] = __float2half_rn(__fmul_rn(gelu_ref(vb), va));
+      break;
+    }
+  }
+}
+
+}  // namespace le

@@ -1,0 +1,349 @@
+"""GPU parity of the CUDA path (through the C ABI) against the CPU oracle.
+
+Tolerances:
+  * dequantised weights: bit-exact (float32 bits);
+  * every embedding: cosine >= 0.99999 and max |diff| <= 2e-3 against the
+    oracle's restatement of the reference's Go forward pass.
+"""
+import os
+import threading
+
+import numpy as np
+import pytest
+
+import oracle
+from llm_embed_b200 import synth
+from llm_embed_b200.embed import Embedder, LlmEmbedError, QWeight, info, init, qgemm
+from helpers import small_spec
+
+pytestmark = pytest.mark.gpu
+
+COS_MIN = 0.99999
+MAX_ABS = 2e-3
+NTHREADS = os.cpu_count() or 8
+
+
+def assert_parity(got, ref, cos_min=COS_MIN, max_abs=MAX_ABS):
+    got = np.asarray(got, np.float32)
+    ref = np.asarray(ref, np.float32)
+    assert got.shape == ref.shape
+    assert np.isfinite(got).all()
+    nz = np.linalg.norm(ref, axis=1) > 0
+    cos = (got * ref).sum(1)[nz] / (np.linalg.norm(got, axis=1)[nz] * np.linalg.norm(ref, axis=1)[nz])
+    err = np.abs(got - ref).max() if got.size else 0.0
+    assert (cos.min() if cos.size else 1.0) >= cos_min, f"min cosine {cos.min():.8f}"
+    assert err <= max_abs, f"max abs diff {err:.3e}"
+    return cos, err
+
+
+@pytest.fixture(scope="module")
+def ndev():
+    return init()
+
+
+def test_init_and_info(ndev):
+    assert ndev >= 1
+    s = info()
+    assert '"arch": "sm_100a"' in s
+
+
+# ------------------------------------------------------------ dequant -----
+
+@pytest.mark.parametrize("wtype", [synth.GGML_Q8_0, synth.GGML_Q4_K, synth.GGML_Q5_K, synth.GGML_Q6_K])
+def test_dequant_bit_exact(model_path, wtype):
+    """Every weight of a 2-layer model: device dequant == DequantWeightMatrix
+    (gemm.go:221) bit for bit; the fp16 operands == round-to-nearest of it."""
+    path = model_path(small_spec(weight_type=wtype, embd_type=wtype))
+    _, tensors = synth.read_gguf(path)
+    e = Embedder.Load(path)
+    try:
+        for layer in range(2):
+            for which, name in enumerate(synth.WEIGHTS):
+                gtype, dims, data = tensors[f"blk.{layer}.{name}.weight"]
+                K, N = dims
+                ref = oracle.dequant_matrix(gtype, np.frombuffer(data, np.uint8), K, N)
+                got = e.dequant(layer, which, mode=0)
+                assert np.array_equal(got.view(np.uint32), ref.view(np.uint32)), f"{name} layer {layer}"
+                got16 = e.dequant(layer, which, mode=1)
+                ref16 = ref.astype(np.float16).astype(np.float32)
+                assert np.array_equal(got16.view(np.uint32), ref16.view(np.uint32)), f"fp16 {name} layer {layer}"
+    finally:
+        e.Close()
+
+
+def test_dequant_subnormal_scales_present(model_path):
+    """The Q6_K super-scales of N(0, 0.02) weights are fp16 subnormals; the
+    bit-exact test above covers them only if they occur."""
+    path = model_path(small_spec(weight_type=synth.GGML_Q6_K, embd_type=synth.GGML_Q6_K))
+    _, tensors = synth.read_gguf(path)
+    _, _, data = tensors["blk.0.attn_qkv.weight"]
+    d = np.frombuffer(data, np.uint8).reshape(-1, 210)[:, 208:210].copy().view(np.uint16)
+    assert ((d & 0x7C00) == 0).any()
+
+
+# ------------------------------------------------------------ forward -----
+
+def _oracle_embed(path, ids, offs, out_dim=None):
+    m = oracle.Model(path)
+    try:
+        return m.embed_ids(ids, offs, out_dim=out_dim, nthreads=NTHREADS)
+    finally:
+        m.close()
+
+
+def test_config0_single_embed(model_path):
+    """Q8_0 model, batch 1, 8 tokens (seed 0)."""
+    path = model_path("q8_0")
+    ids, offs = synth.config_inputs(0)
+    e = Embedder.Load(path)
+    try:
+        got = e.Embed(ids)
+    finally:
+        e.Close()
+    ref = _oracle_embed(path, ids, offs)
+    assert_parity(got[None], ref)
+
+
+@pytest.mark.parametrize("name,config,nseq", [("q8_0", 2, 24), ("q4_k_m", 3, 6), ("q6_k", 4, 2), ("q5_k", 4, 2)])
+def test_config_parity(model_path, name, config, nseq):
+    """First `nseq` sequences of configs[2..4] on their 12-layer models."""
+    path = model_path(name)
+    ids, offs = synth.config_inputs(config)
+    offs = offs[:nseq + 1]
+    ids = ids[:offs[-1]]
+    e = Embedder.Load(path)
+    try:
+        got = e.EmbedIDs(ids, offs)
+    finally:
+        e.Close()
+    ref = _oracle_embed(path, ids, offs)
+    assert_parity(got, ref)
+
+
+def test_edge_lengths(model_path):
+    """Empty sequence (zero vector), length 1, 2, ragged, and the maximum
+    context length, in one packed call."""
+    spec = small_spec(context=2048)
+    path = model_path(spec)
+    lens = [0, 1, 2, 65, 0, 127, 2048]
+    ids, offs = synth.make_ids(lens, seed=5, vocab=spec.vocab)
+    e = Embedder.Load(path)
+    try:
+        got = e.EmbedIDs(ids, offs)
+    finally:
+        e.Close()
+    ref = _oracle_embed(path, ids, offs)
+    assert np.all(got[0] == 0) and np.all(got[4] == 0)
+    assert_parity(got, ref)
+
+
+def test_context_length_enforced(model_path):
+    spec = small_spec(context=512, seed=12)
+    path = model_path(spec)
+    e = Embedder.Load(path)
+    try:
+        ids, offs = synth.make_ids([513], seed=1, vocab=spec.vocab)
+        with pytest.raises(LlmEmbedError):
+            e.EmbedIDs(ids, offs)
+        ids, offs = synth.make_ids([512], seed=1, vocab=spec.vocab)
+        assert_parity(e.EmbedIDs(ids, offs), _oracle_embed(path, ids, offs))
+    finally:
+        e.Close()
+
+
+@pytest.mark.parametrize("dim", [512, 256, 64, 1])
+def test_matryoshka_truncation(model_path, dim):
+    """SetTargetDim + truncate/renormalise (embedder.go:66-68, :142)."""
+    path = model_path(small_spec())
+    ids, offs = synth.make_ids([9, 33, 70], seed=2, vocab=2048)
+    e = Embedder.Load(path)
+    try:
+        e.SetTargetDim(dim)
+        assert e.Dim() == dim
+        got = e.EmbedIDs(ids, offs)
+    finally:
+        e.Close()
+    ref = _oracle_embed(path, ids, offs, out_dim=dim)
+    assert got.shape == (3, dim)
+    assert np.allclose(np.linalg.norm(got, axis=1), 1.0, atol=1e-5)
+    if dim > 1:
+        assert_parity(got, ref)
+    else:
+        assert np.array_equal(np.sign(got), np.sign(ref))
+
+
+def test_set_target_dim_clamps(model_path):
+    e = Embedder.Load(model_path(small_spec()))
+    try:
+        e.SetTargetDim(10_000)
+        assert e.Dim() == 768
+        e.SetTargetDim(0)
+        assert e.Dim() == 1
+    finally:
+        e.Close()
+
+
+def test_batch_equals_single_bitwise(model_path):
+    """EmbedBatch([x]) == Embed(x) and an 8-sequence batch == 8 singles, bit
+    for bit (embedder_test.go:116-145, :212-253)."""
+    e = Embedder.Load(model_path(small_spec()))
+    try:
+        ids, offs = synth.make_ids([5, 9, 3, 12, 7, 8, 4, 6], seed=3, vocab=2048)
+        seqs = [ids[offs[i]:offs[i + 1]] for i in range(8)]
+        batch = e.EmbedBatch(seqs)
+        for s, b in zip(seqs, batch):
+            one = e.Embed(s)
+            assert np.array_equal(one.view(np.uint32), b.view(np.uint32))
+        assert np.array_equal(e.EmbedBatch([seqs[0]])[0].view(np.uint32), e.Embed(seqs[0]).view(np.uint32))
+    finally:
+        e.Close()
+
+
+def test_concurrent_calls(model_path):
+    """16 threads x 3 calls on one model give the single-thread results
+    (embedder_test.go:255-305)."""
+    e = Embedder.Load(model_path(small_spec()))
+    try:
+        ids, offs = synth.make_ids([11, 40, 7, 90], seed=4, vocab=2048)
+        ref = e.EmbedIDs(ids, offs)
+        errs = []
+
+        def work():
+            try:
+                for _ in range(3):
+                    if not np.array_equal(e.EmbedIDs(ids, offs), ref):
+                        errs.append("mismatch")
+            except Exception as ex:  # noqa: BLE001
+                errs.append(repr(ex))
+
+        th = [threading.Thread(target=work) for _ in range(16)]
+        for t in th:
+            t.start()
+        for t in th:
+            t.join()
+        assert not errs, errs[:3]
+    finally:
+        e.Close()
+
+
+def test_load_from_tensor_descs(model_path):
+    """le_model_load with caller-parsed tensors (the path a Go host that keeps
+    internal/gguf takes) equals le_model_load_gguf bit for bit."""
+    path = model_path(small_spec(weight_type=synth.GGML_Q4_K))
+    kv, tensors = synth.read_gguf(path)
+    from llm_embed_b200.embed import HParams
+    hp = HParams(n_layers=kv["nomic-bert.block_count"][1], hidden=kv["nomic-bert.embedding_length"][1],
+                 ffn=kv["nomic-bert.feed_forward_length"][1], heads=kv["nomic-bert.attention.head_count"][1],
+                 context_length=kv["nomic-bert.context_length"][1],
+                 ln_eps=kv["nomic-bert.attention.layer_norm_epsilon"][1],
+                 rope_base=kv["nomic-bert.rope.freq_base"][1])
+    a = Embedder.LoadTensors([(n, t, d, bytes(b)) for n, (t, d, b) in tensors.items()], hp)
+    b = Embedder.Load(path)
+    try:
+        ids, offs = synth.make_ids([17, 3], seed=6, vocab=2048)
+        assert np.array_equal(a.EmbedIDs(ids, offs), b.EmbedIDs(ids, offs))
+    finally:
+        a.Close()
+        b.Close()
+
+
+def test_errors_are_reported(model_path, tmp_path):
+    e = Embedder.Load(model_path(small_spec()))
+    try:
+        with pytest.raises(LlmEmbedError) as ex:
+            e.EmbedIDs(np.array([101, 5000, 102], np.int32), np.array([0, 3], np.int32))
+        assert "outside vocab" in str(ex.value)
+        with pytest.raises(LlmEmbedError):
+            e.EmbedIDs(np.array([101], np.int32), np.array([0, 1], np.int32), out_dim=0)
+        with pytest.raises(LlmEmbedError):
+            e.EmbedIDs(np.array([101, 102], np.int32), np.array([0, 2, 1], np.int32))
+    finally:
+        e.Close()
+    with pytest.raises(LlmEmbedError) as ex:
+        Embedder.Load(str(tmp_path / "missing.gguf"))
+    assert ex.value.code == -5
+    bad = tmp_path / "bad.gguf"
+    bad.write_bytes(b"GGUF" + b"\0" * 64)
+    with pytest.raises(LlmEmbedError):
+        Embedder.Load(str(bad))
+
+
+def test_multi_device_sharding(model_path, ndev):
+    """le_embed_ids over several replicas == one replica, bit for bit."""
+    if ndev < 2:
+        pytest.skip("one GPU")
+    path = model_path(small_spec())
+    ids, offs = synth.make_ids(list(range(1, 40)), seed=7, vocab=2048)
+    one = Embedder.Load(path)
+    many = Embedder.Load(path, devices=list(range(ndev)))
+    try:
+        assert np.array_equal(one.EmbedIDs(ids, offs), many.EmbedIDs(ids, offs))
+    finally:
+        one.Close()
+        many.Close()
+
+
+# ------------------------------------------------------------ op sweep -----
+
+@pytest.mark.parametrize("qtype", [synth.GGML_Q8_0, synth.GGML_Q6_K, synth.GGML_Q5_K, synth.GGML_Q4_K])
+@pytest.mark.parametrize("M,K,N", [(8, 768, 2304), (512, 3072, 768), (37, 768, 3072)])
+def test_qgemm_vs_oracle(qtype, M, K, N):
+    """configs[1] op sweep at oracle-sized M: le_qgemm against the
+    reference's prepacked GEMM (gemm_avx512.go:67) and fused MatMulBatch
+    (ops.go:418).  Tolerance: per output row cosine >= 0.99999 and
+    max |diff| <= 4e-3 * rms(reference) (fp16 operand rounding)."""
+    rng = np.random.default_rng([0, qtype, M, K, N])
+    w = (rng.standard_normal((N, K), dtype=np.float32) * np.float32(0.02))
+    wq = synth.quantize(w, qtype)
+    x = rng.standard_normal((M, K), dtype=np.float32)
+    got = qgemm(qtype, wq, N, K, x)
+    wd = oracle.dequant_matrix(qtype, wq, K, N)
+    for ref in (oracle.gemm(x, wd, NTHREADS), oracle.matmul_batch(qtype, wq, K, N, x, NTHREADS)):
+        rms = float(np.sqrt((ref ** 2).mean()))
+        assert np.abs(got - ref).max() <= 4e-3 * rms
+        cos = (got * ref).sum(1) / (np.linalg.norm(got, axis=1) * np.linalg.norm(ref, axis=1))
+        assert cos.min() >= COS_MIN
+
+
+def test_qgemm_full_size_vs_torch():
+    """configs[1] at M=32768 (too large for the oracle): the device result
+    against a torch float32 matmul of the exact dequantised weight."""
+    import torch
+    qtype, M, K, N = synth.GGML_Q8_0, 32768, 3072, 3072
+    rng = np.random.default_rng(1)
+    w = rng.standard_normal((N, K), dtype=np.float32) * np.float32(0.02)
+    wq = synth.quantize(w, qtype)
+    x = torch.randn(M, K, device="cuda", generator=torch.Generator("cuda").manual_seed(0))
+    y = torch.empty(M, N, device="cuda")
+    qw = QWeight(qtype, wq, N, K)
+    try:
+        qw.matmul_device(x.data_ptr(), M, y.data_ptr())
+        torch.cuda.synchronize()
+    finally:
+        qw.close()
+    wd = torch.from_numpy(oracle.dequant_matrix(qtype, wq, K, N)).cuda()
+    ref = x @ wd.T
+    rms = ref.pow(2).mean().sqrt().item()
+    assert (y - ref).abs().max().item() <= 4e-3 * rms
+    cos = torch.nn.functional.cosine_similarity(y, ref, dim=1)
+    assert cos.min().item() >= COS_MIN
+
+
+def test_config2_full_batch_properties(model_path):
+    """The full configs[2] batch (256 sequences): unit norms, run-to-run
+    bit-identical, and oracle parity of a sample of its sequences."""
+    path = model_path("q8_0")
+    ids, offs = synth.config_inputs(2)
+    e = Embedder.Load(path)
+    try:
+        a = e.EmbedIDs(ids, offs)
+        b = e.EmbedIDs(ids, offs)
+    finally:
+        e.Close()
+    assert np.array_equal(a, b)
+    assert np.allclose(np.linalg.norm(a, axis=1), 1.0, atol=1e-5)
+    pick = [0, 77, 255]
+    sub_ids = np.concatenate([ids[offs[i]:offs[i + 1]] for i in pick])
+    sub_offs = np.concatenate([[0], np.cumsum([offs[i + 1] - offs[i] for i in pick])]).astype(np.int32)
+    ref = _oracle_embed(path, sub_ids, sub_offs)
+    assert_parity(a[pick], ref)
