@@ -186,7 +186,11 @@ def run_ours(args, rank, world, local_rank):
     d_offs = torch.from_numpy(offs).cuda()
     d_out = torch.empty(nseq, H, device="cuda")
     flush = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")
-    stream = torch.cuda.current_stream()
+    # A dedicated stream: the library launches on it and the timing events
+    # are recorded on it (handle 0 would mean "the model's own stream").
+    stream = torch.cuda.Stream()
+    torch.cuda.set_stream(stream)
+    assert stream.cuda_stream != 0
 
     def step():
         e.embed_device(d_ids.data_ptr(), d_offs.data_ptr(), nseq, T, maxlen, d_out.data_ptr(), stream.cuda_stream)
@@ -214,10 +218,13 @@ def run_ours(args, rank, world, local_rank):
     barrier()
     torch.cuda.synchronize()
     clocks.start()
+    enqueue_s = 0.0
     for i in range(args.steps):
         flush.zero_()
         ev[i][0].record(stream)
+        t0 = time.perf_counter()
         step()
+        enqueue_s += time.perf_counter() - t0
         ev[i][1].record(stream)
     torch.cuda.synchronize()
     barrier()
@@ -311,6 +318,7 @@ def run_ours(args, rank, world, local_rank):
                                            "config": "configs[0], L2 flushed before each call"},
             "roofline": roof,
             "gpu_launches": st["launches"],
+            "host_enqueue_ms_per_step": enqueue_s * 1e3 / args.steps,
             "kernel_ms_per_step": breakdown,
             "clocks": clk,
         }

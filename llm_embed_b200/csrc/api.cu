@@ -822,7 +822,7 @@ int le_dequant(le_model* m, int layer, int which, int mode, float* out) {
   if (which == 2 || which == 3) {
     const int F = m->hp.ffn;
     for (int n = 0; n < F; n++) {
-      const int v = (n / 128) * 256 + (n % 128) + (which == 3 ? 128 : 0);
+      const int v = (n / (TILE_N / 2)) * TILE_N + (n % (TILE_N / 2)) + (which == 3 ? TILE_N / 2 : 0);
       std::memcpy(out + (size_t)n * K, all.data() + (size_t)v * K, (size_t)K * 4);
     }
   } else {

@@ -17,22 +17,22 @@ enum GgmlType : int { T_F32 = 0, T_Q8_0 = 8, T_Q4_K = 12, T_Q5_K = 13, T_Q6_K = 
 // Repacked ("tile-blocked") weight format, built on the device at load time.
 //
 // A weight W[N][K] (GGUF dims [K, N], row n = output feature n) is cut into
-// tiles of TILE_N=256 rows x TILE_K=64 columns.  Each tile is one contiguous,
+// tiles of TILE_N=128 rows x TILE_K=64 columns.  Each tile is one contiguous,
 // 16-byte aligned chunk, chunks ordered [n_tile][k_step]:
-//   [0, 16384)            u8  q[256][64]   q + 128 of the signed integer
+//   [0, 8192)             u8  q[128][64]   q + 128 of the signed integer
 //                                          multiplier of every element
-//   [16384, +META_BYTES)  per-row dequant metadata for the 64 columns:
-//       Q8_0:       half  d[256][2]                   (one per 32-block)
-//       Q4_K, Q5_K: float {d*sc, dmin*m}[256][2]      (one pair per 32-block)
-//       Q6_K:       float d*sc[256][4]                (one per 16-block)
+//   [8192, +META_BYTES)   per-row dequant metadata for the 64 columns:
+//       Q8_0:       half  d[128][2]                   (one per 32-block)
+//       Q4_K, Q5_K: float {d*sc, dmin*m}[128][2]      (one pair per 32-block)
+//       Q6_K:       float d*sc[128][4]                (one per 16-block)
 // The float products are formed exactly as the reference does
 // (quant_q4k.go:54-60, quant_q5k.go:202-208, quant_q6k.go:362-365), so a
 // device dequant from this layout is bit-identical to the reference's.
 // Rows past N are zero (q=0, scales 0).
 // ---------------------------------------------------------------------------
-constexpr int TILE_N = 256;
+constexpr int TILE_N = 128;
 constexpr int TILE_K = 64;
-constexpr int TILE_Q_BYTES = TILE_N * TILE_K;  // 16384
+constexpr int TILE_Q_BYTES = TILE_N * TILE_K;  // 8192
 
 enum QFmt : int { QF_Q8_0 = 0, QF_KMIN = 1, QF_Q6K = 2 };
 

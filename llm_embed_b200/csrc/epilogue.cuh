@@ -27,24 +27,27 @@ struct EpiParams {
   int rope_cols;   // columns [0, rope_cols) get RoPE (= 2 * hidden)
 };
 
-// ops_simd.go:27-43, same operation order.
-__device__ __forceinline__ float gelu_ref(float v) {
-  const float t = __fmul_rn(__fmul_rn(0.7978845608f, v), __fadd_rn(1.0f, __fmul_rn(__fmul_rn(0.044715f, v), v)));
-  const float t2 = __fmul_rn(t, t);
-  float th = __fdiv_rn(__fmul_rn(t, __fadd_rn(27.0f, t2)), __fadd_rn(27.0f, __fmul_rn(9.0f, t2)));
-  if (t > 4.97f) th = 1.0f;
-  else if (t < -4.97f) th = -1.0f;
-  return __fmul_rn(__fmul_rn(0.5f, v), __fadd_rn(1.0f, th));
+// ops_simd.go:27-43: 0.5 v (1 + tanh_r(t)), t = 0.7978845608 v (1 + 0.044715
+// v^2), tanh_r(t) = t (27 + t^2) / (27 + 9 t^2) clamped to +-1 for |t| > 4.97.
+// The quotient uses the fast reciprocal: the result is rounded to fp16 (the
+// next GEMM's operand), far coarser than the few-ulp difference.
+__device__ __forceinline__ float gelu_tanh_rational(float v) {
+  const float t = 0.7978845608f * v * (1.0f + 0.044715f * v * v);
+  const float t2 = t * t;
+  float th = __fdividef(t * (27.0f + t2), 27.0f + 9.0f * t2);
+  th = t > 4.97f ? 1.0f : (t < -4.97f ? -1.0f : th);
+  return 0.5f * v * (1.0f + th);
 }
 
 // Map GEMM output pair index p to virtual rows (a, b) and output columns.
-// EPI_GEGLU: tile t = p/128 holds up rows t*256 + c and gate rows
-// t*256 + 128 + c for output column t*128 + c.  Others: a = 2p, b = 2p+1.
+// EPI_GEGLU: weight tile t = p/64 holds up rows t*128 + c (c < 64) and gate
+// rows t*128 + 64 + c, for output column t*64 + c.  Others: a = 2p, b = 2p+1.
+constexpr int GEGLU_HALF = TILE_N / 2;
 __device__ __forceinline__ void pair_rows(int mode, int p, int* a, int* b) {
   if (mode == EPI_GEGLU) {
-    const int t = p >> 7, c = p & 127;
-    *a = t * 256 + c;
-    *b = *a + 128;
+    const int t = p / GEGLU_HALF, c = p % GEGLU_HALF;
+    *a = t * TILE_N + c;
+    *b = *a + GEGLU_HALF;
   } else {
     *a = 2 * p;
     *b = 2 * p + 1;
@@ -81,9 +84,9 @@ __device__ __forceinline__ void epi_pair(const EpiParams& ep, int m, int a, floa
       break;
     }
     case EPI_GEGLU: {
-      const int col = (a >> 8) * 128 + (a & 127);
+      const int col = (a / TILE_N) * GEGLU_HALF + (a % TILE_N);
       if (col >= ep.N) return;
-      ep.out16[(long)m * ep.ldo + col] = __float2half_rn(__fmul_rn(gelu_ref(vb), va));
+      ep.out16[(long)m * ep.ldo + col] = __float2half_rn(gelu_tanh_rational(vb) * va);
       break;
     }
   }

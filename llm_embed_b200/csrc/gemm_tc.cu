@@ -1,24 +1,25 @@
 // Quantised GEMM on the 5th-generation tensor cores (tcgen05, sm_100a).
 //
 // out = A . W^T with A fp16 [M][K] (tokens) and W the tile-blocked quantised
-// weight (common.cuh).  Persistent kernel, one CTA per SM, 128x256 output
-// tiles, K in 64-column steps:
+// weight (common.cuh).  Persistent kernel, one CTA per SM, 256x128 output
+// tiles (256 tokens x 128 weight rows), K in 64-column steps:
 //
-//   warp 0     producer: TMA 2-D load of the A tile (128 x 64 fp16, 128B
-//              swizzle) and a 1-D bulk copy of the raw quant chunk (256 x 64
+//   warp 0     producer: TMA 2-D load of the A tile (256 x 64 fp16, 128B
+//              swizzle) and a 1-D bulk copy of the raw quant chunk (128 x 64
 //              bytes + scales) into a load stage, both completing on one
 //              mbarrier.
-//   warp 1     allocates 512 TMEM columns (two 128x256 fp32 accumulators)
-//              and one lane issues tcgen05.mma (kind::f16, M=128, N=256,
-//              K=16) four times per K step.
+//   warp 1     allocates 512 TMEM columns and one lane issues tcgen05.mma
+//              (kind::f16, M=128, N=128, K=16): per 16-column sub-step one
+//              MMA for each 128-token half, both reading the same B tile, so
+//              each dequantised weight feeds 256 tokens.
 //   warps 2-5  dequantise the raw chunk into the fp16 B operand (the exact
 //              reference value rounded to fp16, dequant.cuh), written in the
 //              128B-swizzled K-major layout tcgen05 reads.
-//   warps 6-9  epilogue: tcgen05.ld the accumulator (each thread one row),
-//              apply the fused epilogue (epilogue.cuh), store to global.
+//   warps 6-9  epilogue: tcgen05.ld the accumulators (each thread one row of
+//              each half), apply the fused epilogue (epilogue.cuh), store.
 //
-// Accumulators are double-buffered so the epilogue of tile i overlaps the
-// main loop of tile i+1.  Every mbarrier wait is bounded (WAIT_LIMIT_NS); on
+// A tile's two accumulators take 256 TMEM columns; two tiles' worth are
+// allocated so the epilogue of tile i overlaps the main loop of tile i+1.  Every mbarrier wait is bounded (WAIT_LIMIT_NS); on
 // expiry the kernel records DE_TIMEOUT in the status word and every role
 // leaves its loop, so a fault in the pipeline ends the launch instead of
 // hanging the GPU.
@@ -35,14 +36,15 @@ namespace le {
 
 namespace tc {
 
-constexpr int BM = 128, BN = TILE_N, BK = TILE_K;
+constexpr int BM = 256, UM = 128, BN = TILE_N, BK = TILE_K;  // UM: rows per MMA
 constexpr int S_LD = 4;  // load stages (A + raw)
 constexpr int S_B = 2;   // fp16 B stages
-constexpr int A_BYTES = BM * BK * 2;   // 16384
-constexpr int B16_BYTES = BN * BK * 2;  // 32768
+constexpr int A_BYTES = BM * BK * 2;    // 32768
+constexpr int B16_BYTES = BN * BK * 2;  // 16384
 constexpr int NTHREADS = 320;
 constexpr int TMEM_COLS = 512;
-constexpr uint32_t IDESC = (1u << 4) | ((uint32_t)(BN >> 3) << 17) | ((uint32_t)(BM >> 4) << 24);
+constexpr int ACC_COLS = 2 * BN;  // one tile: two 128x128 fp32 accumulators
+constexpr uint32_t IDESC = (1u << 4) | ((uint32_t)(BN >> 3) << 17) | ((uint32_t)(UM >> 4) << 24);
 
 template <int QF>
 struct Layout {
@@ -50,7 +52,8 @@ struct Layout {
   static constexpr int OFF_A = 0;
   static constexpr int OFF_RAW = OFF_A + S_LD * A_BYTES;
   static constexpr int OFF_B16 = ((OFF_RAW + S_LD * RAW + 1023) / 1024) * 1024;
-  static constexpr int OFF_BAR = OFF_B16 + S_B * B16_BYTES;
+  static constexpr int OFF_STAGE = OFF_B16 + S_B * B16_BYTES;  // 4 epilogue warps x 32x33 floats
+  static constexpr int OFF_BAR = OFF_STAGE + 4 * 32 * 33 * 4;
   // barriers: full_ld[S_LD], empty_ld[S_LD], full_b[S_B], empty_b[S_B], tfull[2], tempty[2]
   static constexpr int NBAR = 2 * S_LD + 2 * S_B + 4;
   static constexpr int OFF_MISC = OFF_BAR + NBAR * 8;
@@ -157,74 +160,82 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float* v) {
   for (int i = 0; i < 32; i++) v[i] = __uint_as_float(r[i]);
 }
 
-// Epilogue of one 32-column chunk of one row.  n0: first virtual column of
-// the chunk; v: the 32 accumulator values; for EPI_GEGLU v are the up values
-// and g the gate values of the same output columns.
-__device__ __forceinline__ void epi_chunk(const EpiParams& ep, int m, int n0, const float* v, const float* g) {
+// Epilogue of one 32-row x 32-column block, run by one warp.  Lane l holds
+// row row0 + l of the block in v[] (for EPI_GEGLU: up values in v, gate
+// values of the same output columns in g).  Row-wise math (RoPE pairs,
+// gelu(gate)*up) happens in registers; the block then goes through the
+// warp's shared staging area (32 x 33 floats, conflict-free both ways) so
+// that global loads and stores cover whole 128-byte (f32) or 64-byte (fp16)
+// row segments instead of one row per lane.
+__device__ __forceinline__ void epi_block(const EpiParams& ep, int row0, int n0, float* v, const float* g,
+                                          float* stg) {
+  const int lane = threadIdx.x & 31;
+  const int m = row0 + lane;
+  int col0 = n0;  // first output column of the block
   switch (ep.mode) {
-    case EPI_QKV: {
-      if (n0 >= ep.N) return;
-      float o[32];
-      if (n0 < ep.rope_cols) {
+    case EPI_QKV:
+      if (n0 < ep.rope_cols && m < ep.M) {
         const int i0 = (n0 % ep.head_dim) >> 1;
-        const float* cs = ep.rope_cos + (long)ep.pos[m] * (ep.head_dim >> 1) + i0;
-        const float* sn = ep.rope_sin + (long)ep.pos[m] * (ep.head_dim >> 1) + i0;
+        const float4* cs = reinterpret_cast<const float4*>(ep.rope_cos + (long)ep.pos[m] * (ep.head_dim >> 1) + i0);
+        const float4* sn = reinterpret_cast<const float4*>(ep.rope_sin + (long)ep.pos[m] * (ep.head_dim >> 1) + i0);
 #pragma unroll
-        for (int i = 0; i < 16; i++) {
-          const float c = cs[i], s = sn[i];
-          o[2 * i] = __fsub_rn(__fmul_rn(v[2 * i], c), __fmul_rn(v[2 * i + 1], s));
-          o[2 * i + 1] = __fadd_rn(__fmul_rn(v[2 * i], s), __fmul_rn(v[2 * i + 1], c));
+        for (int q = 0; q < 4; q++) {
+          const float4 c = cs[q], s = sn[q];
+          const float cc[4] = {c.x, c.y, c.z, c.w}, ss[4] = {s.x, s.y, s.z, s.w};
+#pragma unroll
+          for (int i = 0; i < 4; i++) {
+            const float x0 = v[8 * q + 2 * i], x1 = v[8 * q + 2 * i + 1];
+            v[8 * q + 2 * i] = __fsub_rn(__fmul_rn(x0, cc[i]), __fmul_rn(x1, ss[i]));
+            v[8 * q + 2 * i + 1] = __fadd_rn(__fmul_rn(x0, ss[i]), __fmul_rn(x1, cc[i]));
+          }
         }
-      } else {
-#pragma unroll
-        for (int i = 0; i < 32; i++) o[i] = v[i];
-      }
-      uint4* dst = reinterpret_cast<uint4*>(ep.out16 + (long)m * ep.ldo + n0);
-#pragma unroll
-      for (int q = 0; q < 4; q++)
-        dst[q] = make_uint4(pack_half2(o[8 * q], o[8 * q + 1]), pack_half2(o[8 * q + 2], o[8 * q + 3]),
-                            pack_half2(o[8 * q + 4], o[8 * q + 5]), pack_half2(o[8 * q + 6], o[8 * q + 7]));
-      break;
-    }
-    case EPI_RESID: {
-      if (n0 >= ep.N) return;
-      const float4* r = reinterpret_cast<const float4*>(ep.resid + (long)m * ep.ldo + n0);
-      float4* dst = reinterpret_cast<float4*>(ep.out32 + (long)m * ep.ldo + n0);
-#pragma unroll
-      for (int q = 0; q < 8; q++) {
-        const float4 a = r[q];
-        dst[q] = make_float4(__fadd_rn(a.x, v[4 * q]), __fadd_rn(a.y, v[4 * q + 1]), __fadd_rn(a.z, v[4 * q + 2]),
-                             __fadd_rn(a.w, v[4 * q + 3]));
       }
       break;
-    }
-    case EPI_GEGLU: {
-      const int col = (n0 >> 8) * 128 + (n0 & 127);
-      if (col >= ep.N) return;
-      uint4* dst = reinterpret_cast<uint4*>(ep.out16 + (long)m * ep.ldo + col);
+    case EPI_GEGLU:
 #pragma unroll
-      for (int q = 0; q < 4; q++) {
-        float o[8];
-#pragma unroll
-        for (int i = 0; i < 8; i++) o[i] = __fmul_rn(gelu_ref(g[8 * q + i]), v[8 * q + i]);
-        dst[q] = make_uint4(pack_half2(o[0], o[1]), pack_half2(o[2], o[3]), pack_half2(o[4], o[5]),
-                            pack_half2(o[6], o[7]));
-      }
+      for (int i = 0; i < 32; i++) v[i] = gelu_tanh_rational(g[i]) * v[i];
+      col0 = (n0 / TILE_N) * GEGLU_HALF + (n0 % TILE_N);
       break;
-    }
-    default: {  // EPI_F32
-      float* dst = ep.out32 + (long)m * ep.ldo + n0;
-      if (n0 + 32 <= ep.N && (ep.ldo & 3) == 0) {
+    default:
+      break;
+  }
 #pragma unroll
-        for (int q = 0; q < 8; q++)
-          reinterpret_cast<float4*>(dst)[q] = make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
-      } else {
+  for (int j = 0; j < 32; j++) stg[lane * 33 + j] = v[j];
+  __syncwarp();
+  if (ep.mode == EPI_QKV || ep.mode == EPI_GEGLU) {
+    // fp16 out: two rows per instruction, lane pairs of columns.
+    const int hr = lane >> 4, c = 2 * (lane & 15);
+    if (col0 + c < ep.N) {
+#pragma unroll 4
+      for (int i = 0; i < 32; i += 2) {
+        const int r = i + hr;
+        if (row0 + r < ep.M)
+          *reinterpret_cast<uint32_t*>(ep.out16 + (long)(row0 + r) * ep.ldo + col0 + c) =
+              pack_half2(stg[r * 33 + c], stg[r * 33 + c + 1]);
+      }
+    }
+  } else {
+    const int col = col0 + lane;
+    if (col < ep.N) {
+      const int nrow = min(32, ep.M - row0);
+      float* out = ep.out32 + (long)row0 * ep.ldo + col;
+      if (ep.mode == EPI_RESID) {
+        // resid may alias out: read the whole block before the first store.
+        const float* rp = ep.resid + (long)row0 * ep.ldo + col;
+        float r[32];
+#pragma unroll
+        for (int i = 0; i < 32; i++) r[i] = i < nrow ? rp[(long)i * ep.ldo] : 0.f;
+#pragma unroll
         for (int i = 0; i < 32; i++)
-          if (n0 + i < ep.N) dst[i] = v[i];
+          if (i < nrow) out[(long)i * ep.ldo] = __fadd_rn(r[i], stg[i * 33 + lane]);
+      } else {
+#pragma unroll 8
+        for (int i = 0; i < 32; i++)
+          if (i < nrow) out[(long)i * ep.ldo] = stg[i * 33 + lane];
       }
-      break;
     }
   }
+  __syncwarp();
 }
 
 template <int QF>
@@ -303,7 +314,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         const uint32_t ar = tcount >> 1;
         if (!mbar_wait(tempty(acc), (ar & 1) ^ 1, abort_flag, status, 2)) break;
         tc_fence_after();
-        const uint32_t d = tmem + acc * BN;
+        const uint32_t d = tmem + acc * ACC_COLS;
         bool ok = true;
         for (int ks = 0; ks < ksteps; ks++, it++, jt++) {
           const int s = it % S_LD, j = jt % S_B;
@@ -316,8 +327,11 @@ __global__ void __launch_bounds__(NTHREADS, 1)
           const uint32_t a_addr = sbase + Lay::OFF_A + s * A_BYTES;
           const uint32_t b_addr = sbase + Lay::OFF_B16 + j * B16_BYTES;
 #pragma unroll
-          for (int kk = 0; kk < BK / 16; kk++)
-            mma_f16(d, sw128_desc(a_addr + kk * 32), sw128_desc(b_addr + kk * 32), (ks | kk) != 0);
+          for (int kk = 0; kk < BK / 16; kk++) {
+            const uint64_t bdesc = sw128_desc(b_addr + kk * 32);
+            mma_f16(d, sw128_desc(a_addr + kk * 32), bdesc, (ks | kk) != 0);
+            mma_f16(d + BN, sw128_desc(a_addr + UM * 128 + kk * 32), bdesc, (ks | kk) != 0);
+          }
           mma_commit(empty_ld(s));
           mma_commit(empty_b(j));
         }
@@ -328,7 +342,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
   } else if (warp < 6) {
     // ------------------------------------------------------------ dequant
     const int t = threadIdx.x - 64;  // 0..127
-    const int g = t & 7, r0 = t >> 3;
+    const int c16 = t & 3, r0 = t >> 2;  // 16-byte column chunk, first row
     uint32_t it = 0, jt = 0;
     bool ok = true;
     for (int tile = blockIdx.x; tile < total && ok; tile += gridDim.x) {
@@ -342,11 +356,15 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         }
         const uint8_t* raw = smem + Lay::OFF_RAW + s * Lay::RAW;
         uint8_t* b16 = smem + Lay::OFF_B16 + j * B16_BYTES;
-#pragma unroll 4
-        for (int q = 0; q < BN / 16; q++) {
-          const int n = r0 + 16 * q;
-          const uint2 u = *reinterpret_cast<const uint2*>(raw + n * BK + g * 8);
-          *reinterpret_cast<uint4*>(b16 + n * 128 + ((g ^ (n & 7)) << 4)) = dq8_f16<QF>(u, raw + TILE_Q_BYTES, n, g);
+#pragma unroll
+        for (int q = 0; q < BN / 32; q++) {
+          const int n = r0 + 32 * q;
+          const uint4 u = *reinterpret_cast<const uint4*>(raw + n * BK + c16 * 16);
+          const int g0 = 2 * c16, sw = n & 7;
+          *reinterpret_cast<uint4*>(b16 + n * 128 + ((g0 ^ sw) << 4)) =
+              dq8_f16<QF>(make_uint2(u.x, u.y), raw + TILE_Q_BYTES, n, g0);
+          *reinterpret_cast<uint4*>(b16 + n * 128 + (((g0 + 1) ^ sw) << 4)) =
+              dq8_f16<QF>(make_uint2(u.z, u.w), raw + TILE_Q_BYTES, n, g0 + 1);
         }
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
         asm volatile("bar.sync 1, 128;" ::: "memory");
@@ -366,20 +384,24 @@ __global__ void __launch_bounds__(NTHREADS, 1)
       if (!__all_sync(0xffffffffu, w)) break;  // warp-uniform: tcgen05.ld is .sync.aligned
       tc_fence_after();
       const int mt = tile / n_tiles, nt = tile % n_tiles;
-      const int m = mt * BM + quarter * 32 + lane;
-      const uint32_t tbase = tmem + acc * BN + ((uint32_t)(quarter * 32) << 16);
-      if (ep.mode == EPI_GEGLU) {
-        for (int c = 0; c < BN / 2; c += 32) {
-          float v[32], gt[32];
-          tmem_ld32(tbase + c, v);
-          tmem_ld32(tbase + BN / 2 + c, gt);
-          if (m < ep.M) epi_chunk(ep, m, nt * BN + c, v, gt);
-        }
-      } else {
-        for (int c = 0; c < BN; c += 32) {
-          float v[32];
-          tmem_ld32(tbase + c, v);
-          if (m < ep.M) epi_chunk(ep, m, nt * BN + c, v, nullptr);
+      float* stg = reinterpret_cast<float*>(smem + Lay::OFF_STAGE) + (warp - 6) * 32 * 33;
+      for (int h = 0; h < BM / UM; h++) {
+        const int row0 = mt * BM + h * UM + quarter * 32;
+        const uint32_t tbase = tmem + acc * ACC_COLS + h * BN + ((uint32_t)(quarter * 32) << 16);
+        if (row0 >= ep.M) continue;  // warp-uniform
+        if (ep.mode == EPI_GEGLU) {
+          for (int c = 0; c < BN / 2; c += 32) {
+            float v[32], gt[32];
+            tmem_ld32(tbase + c, v);
+            tmem_ld32(tbase + BN / 2 + c, gt);
+            epi_block(ep, row0, nt * BN + c, v, gt, stg);
+          }
+        } else {
+          for (int c = 0; c < BN; c += 32) {
+            float v[32];
+            tmem_ld32(tbase + c, v);
+            epi_block(ep, row0, nt * BN + c, v, nullptr, stg);
+          }
         }
       }
       tc_fence_before();

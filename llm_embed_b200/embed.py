@@ -207,7 +207,9 @@ class Embedder:
 
     def embed_device(self, d_ids: int, d_offsets: int, nseq: int, n_tokens: int, max_len: int, d_out: int,
                      stream: int = 0, replica: int = 0, out_dim: int | None = None) -> None:
-        """Asynchronous forward on device pointers of replica `replica`."""
+        """Asynchronous forward on device pointers of replica `replica`,
+        enqueued on the cudaStream_t handle `stream` (0: the model's own
+        stream, which does not order with the legacy default stream)."""
         d = self.target_dim if out_dim is None else out_dim
         _check(lib().le_embed_ids_device(self._handles[replica], d_ids, d_offsets, nseq, n_tokens, max_len, d,
                                          d_out, stream or None))
