@@ -23,6 +23,8 @@ LIB = os.path.join(HERE, "libllmembed_cuda.so")
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 NVFLAGS = ARCH + ["-O3", "-lineinfo", "-std=c++17", "--expt-relaxed-constexpr", "-Xcompiler", "-fPIC",
                   "-Xptxas", "-warn-spills", "-I", os.path.join(HERE, "..", "include")]
+# Extra nvcc flags (e.g. -DLE_TC_S_B=3 to build a pipeline-depth variant).
+NVFLAGS += os.environ.get("LLMEMBED_NVCC_FLAGS", "").split()
 
 
 def _nvcc() -> str:

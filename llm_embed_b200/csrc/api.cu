@@ -133,7 +133,7 @@ struct Layer {
 
 struct Workspace {
   int cap_tokens = 0, cap_seqs = 0;
-  DevBuf ids, offsets, pos, h32, hA, qkv, att, ff, out;
+  DevBuf ids, offsets, pos, h32, y32, hA, qkv, att, ff, out;
   HostBuf h_ids, h_offsets, h_out;
 };
 
@@ -240,7 +240,8 @@ static int make_qmat(QMat& q, int type, const void* src0, const void* src1, int 
   q.qf = qfmt_of(type);
   q.K = K;
   q.n_real = interleave ? 2 * N : N;
-  const int n_tiles = interleave ? (N + TILE_N / 2 - 1) / (TILE_N / 2) : (N + TILE_N - 1) / TILE_N;
+  int n_tiles = interleave ? (N + TILE_N / 2 - 1) / (TILE_N / 2) : (N + TILE_N - 1) / TILE_N;
+  n_tiles += n_tiles & 1;  // even: the CTA-pair GEMM takes weight tiles two at a time
   q.n_virt = n_tiles * TILE_N;
   q.interleaved = interleave;
   TRY(q.buf.ensure((size_t)n_tiles * (K / TILE_K) * chunk_bytes(q.qf)));
@@ -273,6 +274,7 @@ static int ensure_ws(le_model* m, int tokens, int seqs) {
     TRY(w.ids.ensure(T * 4));
     TRY(w.pos.ensure(T * 4));
     TRY(w.h32.ensure(T * H * 4));
+    TRY(w.y32.ensure(T * H * 4));
     TRY(w.hA.ensure(T * H * 2));
     TRY(w.qkv.ensure(T * 3 * H * 2));
     TRY(w.att.ensure(T * H * 2));
@@ -315,6 +317,7 @@ static int forward(le_model* m, const int32_t* d_ids, const int32_t* d_offsets, 
   const int H = m->hp.hidden, F = m->hp.ffn;
   Workspace& w = m->ws;
   float* h32 = w.h32.as<float>();
+  float* y32 = w.y32.as<float>();
   __half* hA = w.hA.as<__half>();
   __half* qkv = w.qkv.as<__half>();
   __half* att = w.att.as<__half>();
@@ -341,13 +344,12 @@ static int forward(le_model* m, const int32_t* d_ids, const int32_t* d_offsets, 
       PLAUNCH(4, launch_attention(qkv, d_offsets, nseq, max_len, H, m->hp.heads, m->head_dim, att, s));
       EpiParams r{};
       r.M = T;
-      r.mode = EPI_RESID;
+      r.mode = EPI_F32;
       r.N = H;
-      r.out32 = h32;
-      r.resid = h32;
+      r.out32 = y32;
       r.ldo = H;
       TRY(gemm(m, 1, L.out, att, H, r, s));
-      PLAUNCH(5, launch_ln(h32, L.attn_w.as<float>(), L.attn_b.as<float>(), m->hp.ln_eps, T, H, h32, hA, s));
+      PLAUNCH(5, launch_ln_add(h32, y32, L.attn_w.as<float>(), L.attn_b.as<float>(), m->hp.ln_eps, T, H, h32, hA, s));
       EpiParams g{};
       g.M = T;
       g.mode = EPI_GEGLU;
@@ -356,7 +358,7 @@ static int forward(le_model* m, const int32_t* d_ids, const int32_t* d_offsets, 
       g.ldo = F;
       TRY(gemm(m, 2, L.upgate, hA, H, g, s));
       TRY(gemm(m, 3, L.down, ff, F, r, s));
-      PLAUNCH(5, launch_ln(h32, L.out_w.as<float>(), L.out_b.as<float>(), m->hp.ln_eps, T, H, h32, hA, s));
+      PLAUNCH(5, launch_ln_add(h32, y32, L.out_w.as<float>(), L.out_b.as<float>(), m->hp.ln_eps, T, H, h32, hA, s));
     }
   }
   PLAUNCH(7, launch_pool(h32, d_offsets, nseq, H, out_dim, d_out, s));

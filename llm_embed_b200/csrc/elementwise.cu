@@ -1,6 +1,8 @@
 // Memory-bound kernels of the forward pass: embedding gather + LayerNorm,
 // residual LayerNorm, masked mean-pool + L2 normalise, f32 -> f16.
 //
+// The residual LayerNorm reads h and the projection output y and writes
+// LN(h + y) back to h (float32) and to the fp16 GEMM operand copy.
 // Row kernels use one warp per 768-wide row: 24 floats per lane in float4s,
 // warp-shuffle reductions, no shared memory.
 #include "common.cuh"
@@ -26,7 +28,8 @@ __device__ __forceinline__ double warp_sum_d(double v) {
 constexpr int LN_MAXV = 8;  // float4 per lane -> H <= 1024
 
 template <bool GATHER>
-__global__ void __launch_bounds__(256) ln_rows_kernel(const float* in, const int32_t* __restrict__ ids,
+__global__ void __launch_bounds__(256) ln_rows_kernel(const float* in, const float* __restrict__ add,
+                                                      const int32_t* __restrict__ ids,
                                                       int emb_type, const uint8_t* __restrict__ emb, long emb_row_bytes,
                                                       const float* __restrict__ type0, const float* __restrict__ w,
                                                       const float* __restrict__ b, float eps, int T, int H,
@@ -57,10 +60,16 @@ __global__ void __launch_bounds__(256) ln_rows_kernel(const float* in, const int
       }
     }
   } else {
+    // bert.go:262-266 / 276-280: h += y, then LayerNorm.
     const float* r = in + (long)warp * H;
+    const float* y = add + (long)warp * H;
 #pragma unroll
     for (int i = 0; i < LN_MAXV; i++)
-      if (i < nv) x[i] = *reinterpret_cast<const float4*>(r + (i * 32 + lane) * 4);
+      if (i < nv) {
+        const float4 a = *reinterpret_cast<const float4*>(r + (i * 32 + lane) * 4);
+        const float4 b = *reinterpret_cast<const float4*>(y + (i * 32 + lane) * 4);
+        x[i] = make_float4(__fadd_rn(a.x, b.x), __fadd_rn(a.y, b.y), __fadd_rn(a.z, b.z), __fadd_rn(a.w, b.w));
+      }
   }
   float s = 0.f, ss = 0.f;
 #pragma unroll
@@ -165,17 +174,17 @@ cudaError_t launch_embed_ln(const int32_t* ids, int emb_type, const uint8_t* emb
                             __half* out16, DevStatus* status, cudaStream_t s) {
   if (H % 128 || H > 128 * LN_MAXV) return cudaErrorInvalidValue;
   if (T == 0) return cudaSuccess;
-  ln_rows_kernel<true><<<(T + 7) / 8, 256, 0, s>>>(nullptr, ids, emb_type, emb, emb_row_bytes, type0, w, b, eps, T, H,
+  ln_rows_kernel<true><<<(T + 7) / 8, 256, 0, s>>>(nullptr, nullptr, ids, emb_type, emb, emb_row_bytes, type0, w, b, eps, T, H,
                                                    vocab, status, out32, out16);
   return cudaGetLastError();
 }
 
-cudaError_t launch_ln(const float* in, const float* w, const float* b, float eps, int T, int H, float* out32,
-                      __half* out16, cudaStream_t s) {
+cudaError_t launch_ln_add(const float* in, const float* add, const float* w, const float* b, float eps, int T, int H,
+                          float* out32, __half* out16, cudaStream_t s) {
   if (H % 128 || H > 128 * LN_MAXV) return cudaErrorInvalidValue;
   if (T == 0) return cudaSuccess;
-  ln_rows_kernel<false><<<(T + 7) / 8, 256, 0, s>>>(in, nullptr, 0, nullptr, 0, nullptr, w, b, eps, T, H, 0, nullptr,
-                                                    out32, out16);
+  ln_rows_kernel<false><<<(T + 7) / 8, 256, 0, s>>>(in, add, nullptr, 0, nullptr, 0, nullptr, w, b, eps, T, H, 0,
+                                                    nullptr, out32, out16);
   return cudaGetLastError();
 }
 

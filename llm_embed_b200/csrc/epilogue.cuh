@@ -1,25 +1,25 @@
 // GEMM epilogues shared by every GEMM kernel.  They receive output values in
 // pairs (va, vb) of the GEMM's "virtual" output rows a, b:
-//   EPI_F32    plain float32 store (standalone qgemm op)
+//   EPI_F32    plain float32 store (attention-output and FFN-down
+//              projections, whose residual add h += y is fused into the
+//              following LayerNorm kernel, and the standalone qgemm op)
 //   EPI_QKV    QKV projection: RoPE on the Q and K columns (adjacent pairs
 //              2i, 2i+1 of each head, ops_simd.go:127-137), fp16 store
-//   EPI_RESID  h += acc (bert.go:262-265, 276-279), float32 store
 //   EPI_GEGLU  merged up/gate: gelu(gate) * up (bert.go:431-436), fp16 store
 #pragma once
 #include "common.cuh"
 
 namespace le {
 
-enum EpiMode : int { EPI_F32 = 0, EPI_QKV = 1, EPI_RESID = 2, EPI_GEGLU = 3 };
+enum EpiMode : int { EPI_F32 = 0, EPI_QKV = 1, EPI_GEGLU = 3 };
 
 struct EpiParams {
   int mode;
   int M;           // valid output rows (tokens)
   int N;           // output columns of the real result
-  float* out32;    // EPI_F32, EPI_RESID
+  float* out32;    // EPI_F32
   __half* out16;   // EPI_QKV, EPI_GEGLU
   long ldo;        // leading dimension of out (elements)
-  const float* resid;  // EPI_RESID (may alias out32)
   const int32_t* pos;  // EPI_QKV: position of each token in its sequence
   const float* rope_cos;  // [max_pos][head_dim/2]
   const float* rope_sin;
@@ -75,12 +75,6 @@ __device__ __forceinline__ void epi_pair(const EpiParams& ep, int m, int a, floa
         x1 = __fadd_rn(__fmul_rn(va, s), __fmul_rn(vb, c));
       }
       *reinterpret_cast<uint32_t*>(ep.out16 + (long)m * ep.ldo + a) = pack_half2(x0, x1);
-      break;
-    }
-    case EPI_RESID: {
-      if (a >= ep.N) return;
-      const float2 r = *reinterpret_cast<const float2*>(ep.resid + (long)m * ep.ldo + a);
-      *reinterpret_cast<float2*>(ep.out32 + (long)m * ep.ldo + a) = make_float2(__fadd_rn(r.x, va), __fadd_rn(r.y, vb));
       break;
     }
     case EPI_GEGLU: {

@@ -6,10 +6,13 @@ namespace le {
 
 cudaError_t launch_gemm(int qf, const uint8_t* W, int n_virtual, int K, const __half* A, long lda, const EpiParams& ep,
                         DevStatus* status, cudaStream_t s) {
-  if (ep.M >= TC_MIN_M && n_virtual % TILE_N == 0) return launch_gemm_tc(qf, W, n_virtual, K, A, lda, ep, status, s);
+  if (ep.M >= TC_MIN_M && n_virtual % (2 * TILE_N) == 0)
+    return launch_gemm_tc2(qf, W, n_virtual, K, A, lda, ep, status, s);
   return launch_gemm_simt(qf, W, n_virtual, K, A, lda, ep, s);
 }
 
-const char* gemm_variant_name() { return "tcgen05 kind::f16 128x256 (M>=64), simt weight-streaming (M<64)"; }
+const char* gemm_variant_name() {
+  return "tcgen05 cta_group::2 kind::f16 256x256 CTA-pair tiles (M>=64), simt weight-streaming (M<64)";
+}
 
 }  // namespace le

@@ -19,8 +19,8 @@ cudaError_t launch_gguf_rows(int type, const uint8_t* src, long row_bytes, int n
 cudaError_t launch_embed_ln(const int32_t* ids, int emb_type, const uint8_t* emb, long emb_row_bytes, int vocab,
                             const float* type0, const float* w, const float* b, float eps, int T, int H, float* out32,
                             __half* out16, DevStatus* status, cudaStream_t s);
-cudaError_t launch_ln(const float* in, const float* w, const float* b, float eps, int T, int H, float* out32,
-                      __half* out16, cudaStream_t s);
+cudaError_t launch_ln_add(const float* in, const float* add, const float* w, const float* b, float eps, int T, int H,
+                          float* out32, __half* out16, cudaStream_t s);
 cudaError_t launch_pool(const float* h, const int32_t* offsets, int nseq, int H, int out_dim, float* out,
                         cudaStream_t s);
 cudaError_t launch_f32_to_f16(const float* in, long n, __half* out, cudaStream_t s);
@@ -34,8 +34,8 @@ cudaError_t launch_attention(const __half* qkv, const int32_t* offsets, int nseq
 cudaError_t launch_gemm_simt(int qf, const uint8_t* W, int n_virtual, int K, const __half* A, long lda,
                              const EpiParams& ep, cudaStream_t s);
 
-// gemm_tc.cu
-cudaError_t launch_gemm_tc(int qf, const uint8_t* W, int n_virtual, int K, const __half* A, long lda,
-                           const EpiParams& ep, DevStatus* status, cudaStream_t s);
+// gemm_tc2.cu
+cudaError_t launch_gemm_tc2(int qf, const uint8_t* W, int n_virtual, int K, const __half* A, long lda,
+                            const EpiParams& ep, DevStatus* status, cudaStream_t s);
 
 }  // namespace le
