@@ -6,7 +6,9 @@ namespace le {
 
 cudaError_t launch_gemm(int qf, const uint8_t* W, int n_virtual, int K, const __half* A, long lda, const EpiParams& ep,
                         DevStatus* status, cudaStream_t s) {
-  if (ep.M >= TC_MIN_M && n_virtual % (2 * TILE_N) == 0)
+  // The tensor-core kernel writes through TMA: output rows 16-byte aligned.
+  const bool tma_ok = ep.mode == EPI_F32 ? ep.ldo % 4 == 0 : ep.ldo % 8 == 0;
+  if (ep.M >= TC_MIN_M && n_virtual % (2 * TILE_N) == 0 && tma_ok)
     return launch_gemm_tc2(qf, W, n_virtual, K, A, lda, ep, status, s);
   return launch_gemm_simt(qf, W, n_virtual, K, A, lda, ep, s);
 }

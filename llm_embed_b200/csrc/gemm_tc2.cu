@@ -19,11 +19,13 @@
 //              in the even CTA one lane issues the MMAs and the commits,
 //              which arrive on the barriers of both CTAs.
 //   dequant    raw chunk -> fp16 B operand (exact reference value rounded to
-//              fp16, dequant.cuh) in the 128B-swizzled K-major layout; the
-//              odd CTA's group arrives on the even CTA's barrier.
-//   epilogue   tcgen05.ld of the local accumulator, fused epilogue
-//              (epilogue.cuh), coalesced stores; frees the accumulator on
-//              the even CTA's barrier.
+//              fp16, dequant.cuh) in the 128B-swizzled K-major layout, each
+//              warp for its own rows; the odd CTA's warps arrive on the even
+//              CTA's barrier.
+//   epilogue   tcgen05.ld of the local accumulator, fused epilogue math
+//              (epilogue.cuh), TMA stores of 32-row x 128-byte blocks from
+//              swizzled staging buffers; frees the accumulator on the even
+//              CTA's barrier.
 //
 // Every mbarrier wait is bounded (WAIT_LIMIT_NS); on expiry the kernel
 // records DE_TIMEOUT and all roles leave their loops.  A cluster barrier
@@ -42,7 +44,7 @@ namespace tc2 {
 using namespace tcx;
 
 #ifndef LE_TC2_S_A
-#define LE_TC2_S_A 7
+#define LE_TC2_S_A 6
 #endif
 #ifndef LE_TC2_S_R
 #define LE_TC2_S_R 4
@@ -52,9 +54,6 @@ using namespace tcx;
 #endif
 #ifndef LE_TC2_DQ_WARPS
 #define LE_TC2_DQ_WARPS 8
-#endif
-#ifndef LE_TC2_RELAY
-#define LE_TC2_RELAY 0
 #endif
 #ifndef LE_TC2_EPI_WARPS
 #define LE_TC2_EPI_WARPS 4
@@ -85,20 +84,51 @@ struct Layout {
   static constexpr int OFF_A = 0;
   static constexpr int OFF_B16 = OFF_A + S_A * A_BYTES;
   static constexpr int OFF_RAW = OFF_B16 + S_B * B16_BYTES;
-  static constexpr int OFF_STAGE = OFF_RAW + S_R * RAW;
-  static constexpr int OFF_BAR = OFF_STAGE + EPI_WARPS * 32 * 33 * 4;
-  // full_a empty_a [S_A], full_raw empty_raw [S_R], full_b empty_b dq_done [S_B], tfull tempty [2]
-  static constexpr int NBAR = 2 * S_A + 2 * S_R + 3 * S_B + 4;
+  // Epilogue staging: per epilogue warp two 32-row x 128-byte buffers in the
+  // 128B-swizzled layout of the output tensor map (TMA stores read them).
+  static constexpr int OFF_STAGE = ((OFF_RAW + S_R * RAW + 1023) / 1024) * 1024;
+  static constexpr int OFF_BAR = OFF_STAGE + EPI_WARPS * 2 * 4096;
+  // full_a empty_a [S_A], full_raw empty_raw [S_R], full_b empty_b [S_B], tfull tempty [2]
+  static constexpr int NBAR = 2 * S_A + 2 * S_R + 2 * S_B + 4;
   static constexpr int OFF_MISC = OFF_BAR + NBAR * 8;
   static constexpr int BYTES = OFF_MISC + 16;
   static constexpr int ALLOC = BYTES + 1024;
   static_assert(ALLOC <= 232448, "shared memory budget of one CTA exceeded");
 };
 
+// TMA store of a 32-row block from shared memory (bulk-group completion).
+__device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, uint32_t src, int c0, int c1) {
+  asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];" ::"l"(
+                   reinterpret_cast<uint64_t>(map)),
+               "r"(src), "r"(c0), "r"(c1)
+               : "memory");
+  asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+}
+
+// One warp stages its 32 rows x 128 bytes (words[32] per lane = its row) in
+// buffer `buf` and stores it with one TMA store at (col0, row0).  Buffers
+// alternate; before reuse the store that last read a buffer must be done.
+__device__ __forceinline__ void emit_block(const CUtensorMap* map, uint32_t stage, int& buf, const uint32_t* words,
+                                           int col0, int row0) {
+  const int lane = threadIdx.x & 31;
+  if (lane == 0) asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory");
+  __syncwarp();
+  const uint32_t base = stage + buf * 4096 + lane * 128;
+#pragma unroll
+  for (int q = 0; q < 8; q++)
+    asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(base + ((q ^ (lane & 7)) << 4)), "r"(words[4 * q]),
+                 "r"(words[4 * q + 1]), "r"(words[4 * q + 2]), "r"(words[4 * q + 3])
+                 : "memory");
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+  __syncwarp();
+  if (lane == 0) tma_store_2d(map, stage + buf * 4096, col0, row0);
+  buf ^= 1;
+}
+
 template <int QF>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NTHREADS, 1)
-    gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_a, const uint8_t* __restrict__ W, int K, int m_tiles,
-                     int n_tiles, EpiParams ep, DevStatus* status) {
+    gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_out,
+                     const uint8_t* __restrict__ W, int K, int m_tiles, int n_tiles, EpiParams ep, DevStatus* status) {
   using Lay = Layout<QF>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
@@ -110,9 +140,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NTHREADS, 1)
   auto empty_raw = [&](int r) { return bar0 + 8 * (2 * S_A + S_R + r); };
   auto full_b = [&](int j) { return bar0 + 8 * (2 * S_A + 2 * S_R + j); };
   auto empty_b = [&](int j) { return bar0 + 8 * (2 * S_A + 2 * S_R + S_B + j); };
-  auto dq_done = [&](int j) { return bar0 + 8 * (2 * S_A + 2 * S_R + 2 * S_B + j); };
-  auto tfull = [&](int a) { return bar0 + 8 * (2 * S_A + 2 * S_R + 3 * S_B + a); };
-  auto tempty = [&](int a) { return bar0 + 8 * (2 * S_A + 2 * S_R + 3 * S_B + 2 + a); };
+  auto tfull = [&](int a) { return bar0 + 8 * (2 * S_A + 2 * S_R + 2 * S_B + a); };
+  auto tempty = [&](int a) { return bar0 + 8 * (2 * S_A + 2 * S_R + 2 * S_B + 2 + a); };
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + Lay::OFF_MISC);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + Lay::OFF_MISC + 4);
 
@@ -133,13 +162,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NTHREADS, 1)
       mbar_init(empty_a(s), 1);  // MMA commit
     }
     for (int r = 0; r < S_R; r++) {
-      mbar_init(full_raw(r), 1);   // local producer's expect_tx; local raw bytes
-      mbar_init(empty_raw(r), 1);  // local dequant group
+      mbar_init(full_raw(r), 1);          // local producer's expect_tx; local raw bytes
+      mbar_init(empty_raw(r), DQ_WARPS);  // every local dequant warp
     }
     for (int j = 0; j < S_B; j++) {
-      mbar_init(full_b(j), 2);   // even CTA: its dequant group + the odd CTA's relay
-      mbar_init(empty_b(j), 1);  // MMA commit
-      mbar_init(dq_done(j), 1);  // odd CTA: its dequant group, watched by the relay
+      mbar_init(full_b(j), 2 * DQ_WARPS);  // even CTA: the dequant warps of both CTAs
+      mbar_init(empty_b(j), 1);            // MMA commit
     }
     for (int a = 0; a < 2; a++) {
       mbar_init(tfull(a), 1);                 // MMA commit
@@ -197,25 +225,6 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NTHREADS, 1)
         }
       }
     }
-  } else if (warp == 1 && !leader && LE_TC2_RELAY) {
-    // ------------------------------------------------------------ relay (odd CTA)
-    // Forwards "B stage j written" to the even CTA's full_b[j].  A remote
-    // arrive is a cluster-scope release; issued here it does not hold up the
-    // dequant group.
-    if (lane == 0) {
-      const uint32_t full_b_leader0 = map_to_rank(full_b(0), 0);
-      uint32_t jt = 0;
-      bool ok = true;
-      for (int tile = cluster; tile < total && ok; tile += nclusters)
-        for (int ks = 0; ks < ksteps; ks++, jt++) {
-          const int j = jt % S_B;
-          if (!mbar_wait(dq_done(j), (jt / S_B) & 1, abort_flag, status, 18)) {
-            ok = false;
-            break;
-          }
-          mbar_arrive_cluster(full_b_leader0 + 8 * j);
-        }
-    }
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA (even CTA)
     if (leader && lane == 0) {
@@ -249,9 +258,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NTHREADS, 1)
     }
   } else if (warp >= DQ_WARP0 && warp < EPI_WARP0) {
     // ------------------------------------------------------------ dequant
-    const int t = threadIdx.x - 32 * DQ_WARP0;
-    const int c16 = t & 3, r0 = t >> 2;
-    constexpr int ROWS_PER_PASS = DQ_THREADS / 4;
+    // Each warp owns TILE_N / DQ_WARPS weight rows of the stage and signals
+    // completion itself: no barrier across the dequant warps.
+    constexpr int ROWS_PER_WARP = TILE_N / DQ_WARPS;
+    const int dw = warp - DQ_WARP0;
+    const int c16 = lane & 3;
+    const uint32_t full_b_leader0 = map_to_rank(full_b(0), 0);
     uint32_t it = 0, jt = 0;
     bool ok = true;
     for (int tile = cluster; tile < total && ok; tile += nclusters) {
@@ -259,15 +271,15 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NTHREADS, 1)
         const int s = it % S_R, j = jt % S_B;
         const bool w = mbar_wait(full_raw(s), (it / S_R) & 1, abort_flag, status, 15) &&
                        mbar_wait(empty_b(j), ((jt / S_B) & 1) ^ 1, abort_flag, status, 16);
-        if (!dequant_group_all(w, DQ_THREADS)) {
+        if (!__all_sync(0xffffffffu, w)) {
           ok = false;
           break;
         }
         const uint8_t* raw = smem + Lay::OFF_RAW + s * Lay::RAW;
         uint8_t* b16 = smem + Lay::OFF_B16 + j * B16_BYTES;
 #pragma unroll
-        for (int q = 0; q < TILE_N / ROWS_PER_PASS; q++) {
-          const int n = r0 + ROWS_PER_PASS * q;
+        for (int q = 0; q < ROWS_PER_WARP / 8; q++) {
+          const int n = dw * ROWS_PER_WARP + 8 * q + (lane >> 2);
           const uint4 u = *reinterpret_cast<const uint4*>(raw + n * BK + c16 * 16);
           const int g0 = 2 * c16, sw = n & 7;
           *reinterpret_cast<uint4*>(b16 + n * 128 + ((g0 ^ sw) << 4)) =
@@ -276,22 +288,25 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NTHREADS, 1)
               dq8_f16<QF>(make_uint2(u.z, u.w), raw + TILE_Q_BYTES, n, g0 + 1);
         }
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // generic writes -> tensor-core reads
-        asm volatile("bar.sync 1, %0;" ::"r"(DQ_THREADS) : "memory");
-        if (t == 0) {
+        __syncwarp();
+        if (lane == 0) {
           mbar_arrive(empty_raw(s));
           if (leader) mbar_arrive(full_b(j));
-          else if (LE_TC2_RELAY) mbar_arrive(dq_done(j));
-          else mbar_arrive_cluster(map_to_rank(full_b(j), 0));
+          else mbar_arrive_cluster(full_b_leader0 + 8 * j);
         }
       }
     }
   } else if (warp >= EPI_WARP0) {
     // ------------------------------------------------------------ epilogue
+    // Accumulator rows -> registers (tcgen05.ld, one row per lane), fused
+    // epilogue math, then 128-byte row blocks through a swizzled staging
+    // buffer and a TMA store of the warp's 32 x 128-byte block.
     const int quarter = warp & 3;  // TMEM lanes 32*quarter .. +31
     const int ew = warp - EPI_WARP0;
     const int c_begin = EPI_WARPS == 8 ? (ew >> 2) * TILE_N : 0;
     const int c_end = EPI_WARPS == 8 ? c_begin + TILE_N : PN;
-    float* stg = reinterpret_cast<float*>(smem + Lay::OFF_STAGE) + ew * 32 * 33;
+    const uint32_t stage = sbase + Lay::OFF_STAGE + ew * 2 * 4096;
+    int buf = 0;
     const uint32_t tempty_leader0 = map_to_rank(tempty(0), 0);
     int tcount = 0;
     for (int tile = cluster; tile < total; tile += nclusters, tcount++) {
@@ -303,40 +318,62 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NTHREADS, 1)
       const int row0 = mt * PM + rank * UM + quarter * 32;
       const uint32_t tbase = tmem + acc * PN + ((uint32_t)(quarter * 32) << 16);
       if (row0 < ep.M) {  // warp-uniform
+        uint32_t words[32];
         if (ep.mode == EPI_GEGLU) {
-          // Each 128-column half is one weight tile: up columns c, gate c + 64.
+          // Each 128-column half is one weight tile: up columns c, gate
+          // c + 64; its 64 outputs form one fp16 block.
 #pragma unroll 1
-          for (int c = c_begin; c < c_end; c += (c % TILE_N) + 32 == GEGLU_HALF ? TILE_N - 32 : 32) {
-            float v[32], gt[32];
-            tmem_ld32(tbase + c, v);
-            tmem_ld32(tbase + c + GEGLU_HALF, gt);
-            epi_block(ep, row0, nt * PN + c, v, gt, nullptr, nullptr, stg);
-          }
-        } else if (ep.mode == EPI_QKV && nt * PN < ep.rope_cols) {
-          const int m = min(row0 + lane, ep.M - 1);
-          const float4* cp = reinterpret_cast<const float4*>(ep.rope_cos + (long)ep.pos[m] * 32);
-          const float4* sp = reinterpret_cast<const float4*>(ep.rope_sin + (long)ep.pos[m] * 32);
-          float cs[32], sn[32];
+          for (int c = c_begin; c < c_end; c += TILE_N) {
 #pragma unroll
-          for (int q = 0; q < 8; q++) {
-            const float4 a = cp[q], b = sp[q];
-            cs[4 * q] = a.x; cs[4 * q + 1] = a.y; cs[4 * q + 2] = a.z; cs[4 * q + 3] = a.w;
-            sn[4 * q] = b.x; sn[4 * q + 1] = b.y; sn[4 * q + 2] = b.z; sn[4 * q + 3] = b.w;
+            for (int h = 0; h < 4; h++) {
+              float up[16], gt[16];
+              tmem_ld16(tbase + c + 16 * h, up);
+              tmem_ld16(tbase + c + 16 * h + GEGLU_HALF, gt);
+#pragma unroll
+              for (int i = 0; i < 8; i++)
+                words[8 * h + i] = pack_half2(gelu_tanh_rational(gt[2 * i]) * up[2 * i],
+                                              gelu_tanh_rational(gt[2 * i + 1]) * up[2 * i + 1]);
+            }
+            emit_block(&tmap_out, stage, buf, words, (nt * PN + c) / TILE_N * GEGLU_HALF, row0);
           }
-#pragma unroll 2
+        } else if (ep.mode == EPI_QKV) {
+          // One head (64 columns) per fp16 block; RoPE on Q and K heads.
+          const bool rope = nt * PN < ep.rope_cols;
+          const long prow = (long)ep.pos[min(row0 + lane, ep.M - 1)] * 32;
+#pragma unroll 1
           for (int c = c_begin; c < c_end; c += 64) {
-            float v[32];
-            tmem_ld32(tbase + c, v);
-            epi_block(ep, row0, nt * PN + c, v, nullptr, cs, sn, stg);
-            tmem_ld32(tbase + c + 32, v);
-            epi_block(ep, row0, nt * PN + c + 32, v, nullptr, cs + 16, sn + 16, stg);
+#pragma unroll
+            for (int h = 0; h < 2; h++) {
+              float v[32];
+              tmem_ld32(tbase + c + 32 * h, v);
+              if (rope) {
+                const float4* cp = reinterpret_cast<const float4*>(ep.rope_cos + prow + 16 * h);
+                const float4* sp = reinterpret_cast<const float4*>(ep.rope_sin + prow + 16 * h);
+#pragma unroll
+                for (int q = 0; q < 4; q++) {
+                  const float4 a = cp[q], b = sp[q];
+                  const float cc[4] = {a.x, a.y, a.z, a.w}, ss[4] = {b.x, b.y, b.z, b.w};
+#pragma unroll
+                  for (int i = 0; i < 4; i++) {
+                    const float x0 = v[8 * q + 2 * i], x1 = v[8 * q + 2 * i + 1];
+                    v[8 * q + 2 * i] = __fsub_rn(__fmul_rn(x0, cc[i]), __fmul_rn(x1, ss[i]));
+                    v[8 * q + 2 * i + 1] = __fadd_rn(__fmul_rn(x0, ss[i]), __fmul_rn(x1, cc[i]));
+                  }
+                }
+              }
+#pragma unroll
+              for (int i = 0; i < 16; i++) words[16 * h + i] = pack_half2(v[2 * i], v[2 * i + 1]);
+            }
+            emit_block(&tmap_out, stage, buf, words, nt * PN + c, row0);
           }
         } else {
 #pragma unroll 1
           for (int c = c_begin; c < c_end; c += 32) {
             float v[32];
             tmem_ld32(tbase + c, v);
-            epi_block(ep, row0, nt * PN + c, v, nullptr, nullptr, nullptr, stg);
+#pragma unroll
+            for (int i = 0; i < 32; i++) words[i] = __float_as_uint(v[i]);
+            emit_block(&tmap_out, stage, buf, words, nt * PN + c, row0);
           }
         }
       }
@@ -344,6 +381,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NTHREADS, 1)
       __syncwarp();
       if (lane == 0) mbar_arrive_cluster(tempty_leader0 + 8 * acc);
     }
+    if (lane == 0) asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");  // all stores done
+    __syncwarp();
   }
 
   tc_fence_before();
@@ -389,6 +428,22 @@ cudaError_t launch(const uint8_t* W, int n_virtual, int K, const __half* A, long
           CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
           CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
     return cudaErrorInvalidValue;
+  // Output map: 32-row x 128-byte boxes (32 float32 or 64 fp16 columns),
+  // 128B swizzle as the epilogue stages them.
+  CUtensorMap omap;
+  {
+    const bool f32 = ep.mode == EPI_F32;
+    void* out = f32 ? static_cast<void*>(ep.out32) : static_cast<void*>(ep.out16);
+    const int esz = f32 ? 4 : 2;
+    if ((ep.ldo * esz) % 16 || (reinterpret_cast<uintptr_t>(out) & 15)) return cudaErrorInvalidValue;
+    const cuuint64_t odims[2] = {(cuuint64_t)ep.N, (cuuint64_t)ep.M};
+    const cuuint64_t ostrides[1] = {(cuuint64_t)ep.ldo * esz};
+    const cuuint32_t obox[2] = {(cuuint32_t)(128 / esz), 32};
+    if (enc(&omap, f32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, out, odims, ostrides,
+            obox, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_NONE,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+      return cudaErrorInvalidValue;
+  }
   // Per device: the shared-memory attribute and the number of CTA pairs
   // that can be resident at once (the persistent grid's size).
   static std::mutex mu;
@@ -421,7 +476,7 @@ cudaError_t launch(const uint8_t* W, int n_virtual, int K, const __half* A, long
   const int n_tiles = n_virtual / PN;
   const int total = m_tiles * n_tiles;
   const int pairs = total < max_pairs[dev] ? total : max_pairs[dev];
-  gemm_pair_kernel<QF><<<2 * pairs, NTHREADS, Layout<QF>::ALLOC, s>>>(map, W, K, m_tiles, n_tiles, ep, status);
+  gemm_pair_kernel<QF><<<2 * pairs, NTHREADS, Layout<QF>::ALLOC, s>>>(map, omap, W, K, m_tiles, n_tiles, ep, status);
   return cudaGetLastError();
 }
 
