@@ -4,13 +4,21 @@
 // 10 below the row maximum are exactly 0), weighted sum of V.
 //
 // Q, K, V come RoPE-rotated in fp16 from the QKV GEMM epilogue, laid out as
-// rows of qkv[T][3H]; the output is att[T][H] fp16.  One CTA handles 64
-// queries of one (sequence, head); each of its 4 warps owns 16 queries.
-// Two passes over the keys: the first finds each row's maximum (the cutoff
-// is relative to the final maximum, so an online-softmax rescale would not
-// reproduce it), the second accumulates exp(s - max) and P.V in fp32.
-// Tensor-core math uses mma.sync m16n8k16 (fp16 in, fp32 accumulate).
+// rows of qkv[T][3H]; the output is att[T][H] fp16.  The cutoff is relative
+// to the row's final maximum, so every kernel finds the exact maximum before
+// exponentiating (an online-softmax rescale would not reproduce it).
+// Tensor-core math: mma.sync m16n8k16 (fp16 in, fp32 accumulate), operand
+// fragments loaded with ldmatrix.
+//
+//   attention_short_kernel  L <= 128: one CTA of 4 warps per (64 queries,
+//       head, sequence) keeps K, V of the whole sequence and its Q rows in
+//       shared memory (cp.async); each warp holds its 16 query rows' scores
+//       for all keys in registers (one pass).
+//   attention_long_kernel   L > 128: one CTA per (64 queries, head,
+//       sequence), keys in 64-row blocks, a max pass then an exp + P.V pass.
 #include <math.h>
+
+#include <mutex>
 
 #include "common.cuh"
 #include "kernels.h"
@@ -19,10 +27,13 @@ namespace le {
 
 namespace {
 
-constexpr int QB = 64;   // queries per CTA
-constexpr int KB = 64;   // keys per smem block
 constexpr int HD = 64;   // head dim
-constexpr int LDS = 72;  // smem row stride (halves): 144 B, staggers banks
+constexpr int LDS = 72;  // smem row stride (halves): 144 B keeps ldmatrix rows on distinct banks
+constexpr int SH_MAXL = 128;
+constexpr int SH_QROWS = 64;
+constexpr int SH_WARPS = SH_QROWS / 16;
+constexpr int SH_SMEM = (SH_QROWS + 2 * SH_MAXL) * LDS * 2;
+constexpr int QB = 64, KB = 64;  // long kernel blocks
 
 __device__ __forceinline__ void mma16816(float* c, const uint32_t* a, uint32_t b0, uint32_t b1) {
   asm volatile(
@@ -31,15 +42,21 @@ __device__ __forceinline__ void mma16816(float* c, const uint32_t* a, uint32_t b
       : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
       : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
 }
-
-__device__ __forceinline__ uint32_t ld_h2(const __half* p) { return *reinterpret_cast<const uint32_t*>(p); }
-__device__ __forceinline__ uint32_t pack_h(__half lo, __half hi) {
-  return (uint32_t)__half_as_ushort(lo) | ((uint32_t)__half_as_ushort(hi) << 16);
+__device__ __forceinline__ void ldsm_x4(uint32_t* r, const __half* p) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"((uint32_t)__cvta_generic_to_shared(p)));
+}
+__device__ __forceinline__ void ldsm_x4_t(uint32_t* r, const __half* p) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"((uint32_t)__cvta_generic_to_shared(p)));
 }
 
-// Load rows [r0, r0+64) of one head's 64 columns (zero past `valid` rows).
-__device__ __forceinline__ void load_block(__half (*dst)[LDS], const __half* src, long ld, int r0, int valid) {
-  for (int i = threadIdx.x; i < 64 * 8; i += blockDim.x) {
+// Rows [r0, r0 + n) of one head's 64 columns into dst (zero rows past
+// `valid`), by all threads of the block.
+__device__ __forceinline__ void load_rows(__half (*dst)[LDS], const __half* src, long ld, int r0, int n, int valid) {
+  for (int i = threadIdx.x; i < n * 8; i += blockDim.x) {
     const int r = i >> 3, c = (i & 7) * 8;
     uint4 v = make_uint4(0, 0, 0, 0);
     if (r0 + r < valid) v = *reinterpret_cast<const uint4*>(src + (long)(r0 + r) * ld + c);
@@ -47,48 +64,174 @@ __device__ __forceinline__ void load_block(__half (*dst)[LDS], const __half* src
   }
 }
 
+// Same with cp.async (16-byte, L2 only); the caller waits and syncs.
+__device__ __forceinline__ void load_rows_async(__half (*dst)[LDS], const __half* src, long ld, int r0, int n,
+                                                int valid) {
+  for (int i = threadIdx.x; i < n * 8; i += blockDim.x) {
+    const int r = i >> 3, c = (i & 7) * 8;
+    const uint32_t d = (uint32_t)__cvta_generic_to_shared(&dst[r][c]);
+    if (r0 + r < valid)
+      asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(d), "l"(src + (long)(r0 + r) * ld + c) : "memory");
+    else
+      *reinterpret_cast<uint4*>(&dst[r][c]) = make_uint4(0, 0, 0, 0);
+  }
+}
+
+// A fragments of 16 query rows (row0..row0+15) x 64 dims.
+__device__ __forceinline__ void load_q_frags(uint32_t (*qa)[4], __half (*sQ)[LDS], int row0) {
+  const int lane = threadIdx.x & 31;
+#pragma unroll
+  for (int kc = 0; kc < 4; kc++) ldsm_x4(qa[kc], &sQ[row0 + (lane & 15)][kc * 16 + (lane >> 4) * 8]);
+}
+
+// s += Q(16 x 64) . K(8 keys x 64)^T for keys key0..key0+7.
+__device__ __forceinline__ void qk_tile(float* s, uint32_t (*qa)[4], __half (*sK)[LDS], int key0) {
+  const int lane = threadIdx.x & 31;
+  uint32_t b[8];
+  ldsm_x4(b, &sK[key0 + (lane & 7)][(lane >> 3) * 8]);
+  ldsm_x4(b + 4, &sK[key0 + (lane & 7)][32 + (lane >> 3) * 8]);
+  mma16816(s, qa[0], b[0], b[1]);
+  mma16816(s, qa[1], b[2], b[3]);
+  mma16816(s, qa[2], b[4], b[5]);
+  mma16816(s, qa[3], b[6], b[7]);
+}
+
+// o[8][4] += P(16 x 16 keys) . V(16 keys x 64) for keys key0..key0+15.
+__device__ __forceinline__ void pv_chunk(float (*o)[4], const uint32_t* pa, __half (*sV)[LDS], int key0) {
+  const int lane = threadIdx.x & 31;
+#pragma unroll
+  for (int dt = 0; dt < 8; dt += 2) {
+    uint32_t b[4];
+    ldsm_x4_t(b, &sV[key0 + (lane & 7) + ((lane >> 3) & 1) * 8][8 * dt + (lane >> 4) * 8]);
+    mma16816(o[dt], pa, b[0], b[1]);
+    mma16816(o[dt + 1], pa, b[2], b[3]);
+  }
+}
+
+// exp rule of ops_simd.go:70-82 on a score x already reduced by the max.
+__device__ __forceinline__ float ref_exp(float x) { return x < -10.f ? 0.f : expf(x); }
+
+// Normalise and store 16 rows x 64 dims (rows q0 and q0+8 of this lane).
+__device__ __forceinline__ void store_rows(__half* out, long ldo, int L, int q0, float (*o)[4], float l0, float l1) {
+  const int tq = threadIdx.x & 3;
+  const float inv0 = 1.0f / l0, inv1 = 1.0f / l1;
+#pragma unroll
+  for (int dt = 0; dt < 8; dt++) {
+    const int d = dt * 8 + tq * 2;
+    if (q0 < L) *reinterpret_cast<uint32_t*>(out + (long)q0 * ldo + d) = pack_half2(o[dt][0] * inv0, o[dt][1] * inv0);
+    if (q0 + 8 < L)
+      *reinterpret_cast<uint32_t*>(out + (long)(q0 + 8) * ldo + d) = pack_half2(o[dt][2] * inv1, o[dt][3] * inv1);
+  }
+}
+
 }  // namespace
 
-__global__ void __launch_bounds__(128) attention_kernel(const __half* __restrict__ qkv, const int32_t* __restrict__ offsets,
-                                                        int H, __half* __restrict__ out) {
+__global__ void __launch_bounds__(SH_WARPS * 32) attention_short_kernel(const __half* __restrict__ qkv,
+                                                                       const int32_t* __restrict__ offsets, int H,
+                                                                       __half* __restrict__ out) {
   const int qb = blockIdx.x, head = blockIdx.y, s = blockIdx.z;
   const int t0 = offsets[s];
   const int L = offsets[s + 1] - t0;
-  if (qb * QB >= L) return;
+  if (L == 0 || L > SH_MAXL || qb * SH_QROWS >= L) return;
+  extern __shared__ __align__(16) uint8_t smem_attn[];
+  __half(*sQ)[LDS] = reinterpret_cast<__half(*)[LDS]>(smem_attn);
+  __half(*sK)[LDS] = sQ + SH_QROWS;
+  __half(*sV)[LDS] = sK + SH_MAXL;
+  const long ld = 3L * H;
+  const __half* base = qkv + (long)t0 * ld + head * HD;
+  const int Lp = (L + 15) & ~15;
+  load_rows_async(sQ, base, ld, qb * SH_QROWS, SH_QROWS, L);
+  load_rows_async(sK, base + H, ld, 0, Lp, L);
+  load_rows_async(sV, base + 2 * H, ld, 0, Lp, L);
+  asm volatile("cp.async.wait_all;" ::: "memory");
+  __syncthreads();
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, tq = lane & 3;
+  const int qrow0 = qb * SH_QROWS + warp * 16;
+  if (qrow0 >= L) return;
+  uint32_t qa[4][4];
+  load_q_frags(qa, sQ, warp * 16);
+
+  float sc[SH_MAXL / 8][4];
+#pragma unroll
+  for (int n = 0; n < SH_MAXL / 8; n++) {
+    sc[n][0] = sc[n][1] = sc[n][2] = sc[n][3] = 0.f;
+    if (n * 8 < Lp) qk_tile(sc[n], qa, sK, n * 8);
+  }
+  float mx0 = -INFINITY, mx1 = -INFINITY;
+#pragma unroll
+  for (int n = 0; n < SH_MAXL / 8; n++) {
+    const int key = n * 8 + tq * 2;
+#pragma unroll
+    for (int j = 0; j < 4; j++) {
+      const float v = (key + (j & 1) < L) ? sc[n][j] * 0.125f : -INFINITY;
+      sc[n][j] = v;
+      if (j < 2) mx0 = fmaxf(mx0, v);
+      else mx1 = fmaxf(mx1, v);
+    }
+  }
+#pragma unroll
+  for (int o = 1; o <= 2; o <<= 1) {
+    mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, o));
+    mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, o));
+  }
+  float l0 = 0.f, l1 = 0.f;
+#pragma unroll
+  for (int n = 0; n < SH_MAXL / 8; n++) {
+    sc[n][0] = ref_exp(__fsub_rn(sc[n][0], mx0));
+    sc[n][1] = ref_exp(__fsub_rn(sc[n][1], mx0));
+    sc[n][2] = ref_exp(__fsub_rn(sc[n][2], mx1));
+    sc[n][3] = ref_exp(__fsub_rn(sc[n][3], mx1));
+    l0 += sc[n][0] + sc[n][1];
+    l1 += sc[n][2] + sc[n][3];
+  }
+#pragma unroll
+  for (int o = 1; o <= 2; o <<= 1) {
+    l0 += __shfl_xor_sync(0xffffffffu, l0, o);
+    l1 += __shfl_xor_sync(0xffffffffu, l1, o);
+  }
+  float acc[8][4];
+#pragma unroll
+  for (int i = 0; i < 8; i++) acc[i][0] = acc[i][1] = acc[i][2] = acc[i][3] = 0.f;
+#pragma unroll
+  for (int c = 0; c < SH_MAXL / 16; c++) {
+    if (c * 16 < Lp) {
+      const uint32_t pa[4] = {pack_half2(sc[2 * c][0], sc[2 * c][1]), pack_half2(sc[2 * c][2], sc[2 * c][3]),
+                              pack_half2(sc[2 * c + 1][0], sc[2 * c + 1][1]),
+                              pack_half2(sc[2 * c + 1][2], sc[2 * c + 1][3])};
+      pv_chunk(acc, pa, sV, c * 16);
+    }
+  }
+  store_rows(out + (long)t0 * H + head * HD, H, L, qrow0 + g, acc, l0, l1);
+}
+
+__global__ void __launch_bounds__(128) attention_long_kernel(const __half* __restrict__ qkv,
+                                                             const int32_t* __restrict__ offsets, int H,
+                                                             __half* __restrict__ out) {
+  const int qb = blockIdx.x, head = blockIdx.y, s = blockIdx.z;
+  const int t0 = offsets[s];
+  const int L = offsets[s + 1] - t0;
+  if (L <= SH_MAXL || qb * QB >= L) return;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, tq = lane & 3;
   __shared__ __align__(16) __half sQ[QB][LDS];
   __shared__ __align__(16) __half sK[KB][LDS];
   __shared__ __align__(16) __half sV[KB][LDS];
   const long ld = 3L * H;
   const __half* base = qkv + (long)t0 * ld + head * HD;
-
-  load_block(sQ, base, ld, qb * QB, L);
+  load_rows(sQ, base, ld, qb * QB, QB, L);
   __syncthreads();
   uint32_t qa[4][4];
-  {
-    const int r0 = warp * 16 + g;
-#pragma unroll
-    for (int kc = 0; kc < 4; kc++) {
-      const int c0 = kc * 16 + tq * 2;
-      qa[kc][0] = ld_h2(&sQ[r0][c0]);
-      qa[kc][1] = ld_h2(&sQ[r0 + 8][c0]);
-      qa[kc][2] = ld_h2(&sQ[r0][c0 + 8]);
-      qa[kc][3] = ld_h2(&sQ[r0 + 8][c0 + 8]);
-    }
-  }
+  load_q_frags(qa, sQ, warp * 16);
 
   // Pass 1: row maxima of the scaled scores.
   float mx0 = -INFINITY, mx1 = -INFINITY;
   for (int kb = 0; kb < L; kb += KB) {
     __syncthreads();
-    load_block(sK, base + H, ld, kb, L);
+    load_rows(sK, base + H, ld, kb, KB, L);
     __syncthreads();
 #pragma unroll
     for (int nt = 0; nt < KB / 8; nt++) {
       float c[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-      for (int kc = 0; kc < 4; kc++)
-        mma16816(c, qa[kc], ld_h2(&sK[nt * 8 + g][kc * 16 + tq * 2]), ld_h2(&sK[nt * 8 + g][kc * 16 + tq * 2 + 8]));
+      qk_tile(c, qa, sK, nt * 8);
       const int key = kb + nt * 8 + tq * 2;
       if (key < L) {
         mx0 = fmaxf(mx0, c[0] * 0.125f);
@@ -113,8 +256,8 @@ __global__ void __launch_bounds__(128) attention_kernel(const __half* __restrict
   for (int i = 0; i < 8; i++) acc[i][0] = acc[i][1] = acc[i][2] = acc[i][3] = 0.f;
   for (int kb = 0; kb < L; kb += KB) {
     __syncthreads();
-    load_block(sK, base + H, ld, kb, L);
-    load_block(sV, base + 2 * H, ld, kb, L);
+    load_rows(sK, base + H, ld, kb, KB, L);
+    load_rows(sV, base + 2 * H, ld, kb, KB, L);
     __syncthreads();
 #pragma unroll
     for (int kc2 = 0; kc2 < KB / 16; kc2++) {
@@ -123,32 +266,19 @@ __global__ void __launch_bounds__(128) attention_kernel(const __half* __restrict
       for (int h2 = 0; h2 < 2; h2++) {
         const int nt = kc2 * 2 + h2;
         float c[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-        for (int kc = 0; kc < 4; kc++)
-          mma16816(c, qa[kc], ld_h2(&sK[nt * 8 + g][kc * 16 + tq * 2]), ld_h2(&sK[nt * 8 + g][kc * 16 + tq * 2 + 8]));
+        qk_tile(c, qa, sK, nt * 8);
         const int key = kb + nt * 8 + tq * 2;
 #pragma unroll
         for (int j = 0; j < 4; j++) {
           const bool valid = key + (j & 1) < L;
-          const float x = __fsub_rn(c[j] * 0.125f, (j < 2) ? mx0 : mx1);
-          p[h2][j] = (valid && !(x < -10.f)) ? expf(x) : 0.f;
+          p[h2][j] = valid ? ref_exp(__fsub_rn(c[j] * 0.125f, (j < 2) ? mx0 : mx1)) : 0.f;
         }
         l0 += p[h2][0] + p[h2][1];
         l1 += p[h2][2] + p[h2][3];
       }
-      uint32_t pa[4];
-      pa[0] = pack_half2(p[0][0], p[0][1]);
-      pa[1] = pack_half2(p[0][2], p[0][3]);
-      pa[2] = pack_half2(p[1][0], p[1][1]);
-      pa[3] = pack_half2(p[1][2], p[1][3]);
-      const int kr = kc2 * 16 + tq * 2;
-#pragma unroll
-      for (int dt = 0; dt < 8; dt++) {
-        const int d = dt * 8 + g;
-        const uint32_t b0 = pack_h(sV[kr][d], sV[kr + 1][d]);
-        const uint32_t b1 = pack_h(sV[kr + 8][d], sV[kr + 9][d]);
-        mma16816(acc[dt], pa, b0, b1);
-      }
+      const uint32_t pa[4] = {pack_half2(p[0][0], p[0][1]), pack_half2(p[0][2], p[0][3]),
+                              pack_half2(p[1][0], p[1][1]), pack_half2(p[1][2], p[1][3])};
+      pv_chunk(acc, pa, sV, kc2 * 16);
     }
   }
 #pragma unroll
@@ -156,25 +286,37 @@ __global__ void __launch_bounds__(128) attention_kernel(const __half* __restrict
     l0 += __shfl_xor_sync(0xffffffffu, l0, o);
     l1 += __shfl_xor_sync(0xffffffffu, l1, o);
   }
-  const float inv0 = 1.0f / l0, inv1 = 1.0f / l1;
-  const int q0 = qb * QB + warp * 16 + g;
-  __half* o0 = out + (long)(t0 + q0) * H + head * HD;
-  __half* o1 = o0 + 8L * H;
-#pragma unroll
-  for (int dt = 0; dt < 8; dt++) {
-    const int d = dt * 8 + tq * 2;
-    if (q0 < L) *reinterpret_cast<uint32_t*>(o0 + d) = pack_half2(acc[dt][0] * inv0, acc[dt][1] * inv0);
-    if (q0 + 8 < L) *reinterpret_cast<uint32_t*>(o1 + d) = pack_half2(acc[dt][2] * inv1, acc[dt][3] * inv1);
-  }
+  store_rows(out + (long)t0 * H + head * HD, H, L, qb * QB + warp * 16 + g, acc, l0, l1);
 }
 
 cudaError_t launch_attention(const __half* qkv, const int32_t* offsets, int nseq, int max_len, int H, int heads,
                              int head_dim, __half* out, cudaStream_t s) {
   if (head_dim != HD) return cudaErrorInvalidValue;
   if (nseq == 0 || max_len == 0) return cudaSuccess;
-  for (int s0 = 0; s0 < nseq; s0 += 65535) {  // grid.z limit
-    dim3 grid((max_len + QB - 1) / QB, heads, nseq - s0 < 65535 ? nseq - s0 : 65535);
-    attention_kernel<<<grid, 128, 0, s>>>(qkv, offsets + s0, H, out);
+  static std::mutex mu;
+  static uint64_t attr_set = 0;  // per-device bit: the attribute is a per-device setting
+  int dev = 0;
+  cudaGetDevice(&dev);
+  {
+    std::lock_guard<std::mutex> lk(mu);
+    if (dev >= 64 || !(attr_set >> dev & 1)) {
+      cudaError_t e =
+          cudaFuncSetAttribute(attention_short_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SH_SMEM);
+      if (e == cudaSuccess)
+        e = cudaFuncSetAttribute(attention_short_kernel, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
+      if (e == cudaSuccess)
+        e = cudaFuncSetAttribute(attention_long_kernel, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
+      if (e != cudaSuccess) return e;
+      if (dev < 64) attr_set |= 1ull << dev;
+    }
+  }
+  for (int s0 = 0; s0 < nseq; s0 += 65535) {  // grid.y/z limit
+    const int n = nseq - s0 < 65535 ? nseq - s0 : 65535;
+    const int sq = (max_len < SH_MAXL ? max_len : SH_MAXL);
+    attention_short_kernel<<<dim3((sq + SH_QROWS - 1) / SH_QROWS, heads, n), SH_WARPS * 32, SH_SMEM, s>>>(
+        qkv, offsets + s0, H, out);
+    if (max_len > SH_MAXL)
+      attention_long_kernel<<<dim3((max_len + QB - 1) / QB, heads, n), 128, 0, s>>>(qkv, offsets + s0, H, out);
   }
   return cudaGetLastError();
 }
