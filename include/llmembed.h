@@ -130,6 +130,19 @@ int le_qweight_create(int dev, int qtype, const void* wq, int N, int K, le_qweig
 int le_qgemm_device(le_qweight* w, const float* d_x, int M, float* d_y, void* stream);
 int le_qweight_free(le_qweight* w);
 
+/* le_qgemm_device without allocation (no counterpart in the reference: its Go
+ * GEMM allocates per call; this entry point exists for callers that must not
+ * allocate device memory, e.g. inside a caller-managed memory budget).  The
+ * fp16 copy of x and the kernel status word live in one file-scope device
+ * array of 256 + 2*LE_QGEMM_NOALLOC_MAX_ELEMS bytes per device, so M*K must
+ * not exceed LE_QGEMM_NOALLOC_MAX_ELEMS (LE_EINVAL otherwise).  The call
+ * calls no cudaMalloc/cudaFree, runs on `stream` (NULL = the weight's
+ * stream), waits for it and returns LE_EDEVICE on a kernel-reported failure.
+ * Every call on a device shares the array: calls whose work overlaps on the
+ * GPU (other streams, other host threads) race on it. */
+#define LE_QGEMM_NOALLOC_MAX_ELEMS (4 * 1024 * 1024)
+int le_qgemm_device_noalloc(le_qweight* w, const float* d_x, int M, float* d_y, void* stream);
+
 /* Per-kernel device timing of le_embed_ids / le_embed_ids_device calls.
  * With profiling on, every kernel launch of the forward pass is bracketed by
  * CUDA events on its stream; le_get_stats synchronises and returns the

@@ -891,6 +891,64 @@ int le_qgemm(int dev, int qtype, const void* wq, int N, int K, const float* x, i
   return check_status(w->status, w->stream);
 }
 
+// le_qgemm_device_noalloc: le_qgemm_device with its scratch (the status word
+// and the fp16 copy of x) in one file-scope device array instead of buffers
+// grown per weight.  Layout: [0, 256) DevStatus, then fp16 x [M][K].  The
+// array is shared by every call on a device; only the status word has to
+// start at zero, and each call clears it first.
+static __device__ __align__(256) uint8_t g_noalloc_scratch[256 + (size_t)LE_QGEMM_NOALLOC_MAX_ELEMS * 2];
+
+constexpr int NOALLOC_MAX_DEVICES = 64;
+static std::mutex g_noalloc_mu;
+static void* g_noalloc_ptr[NOALLOC_MAX_DEVICES];
+
+// Device address of the scratch array on the current device `dev`, looked up
+// once per device.
+static int noalloc_scratch(int dev, uint8_t** out) {
+  if (dev < 0 || dev >= NOALLOC_MAX_DEVICES) return fail(LE_EINVAL, "device %d beyond %d", dev, NOALLOC_MAX_DEVICES);
+  std::lock_guard<std::mutex> lk(g_noalloc_mu);
+  if (!g_noalloc_ptr[dev]) {
+    void* p = nullptr;
+    CK(cudaGetSymbolAddress(&p, g_noalloc_scratch));
+    if (!p || reinterpret_cast<uintptr_t>(p) % 256) return fail(LE_ECUDA, "scratch array address %p", p);
+    g_noalloc_ptr[dev] = p;
+  }
+  *out = static_cast<uint8_t*>(g_noalloc_ptr[dev]);
+  return LE_OK;
+}
+
+int le_qgemm_device_noalloc(le_qweight* w, const float* d_x, int M, float* d_y, void* stream) {
+  if (!w || (M > 0 && (!d_x || !d_y))) return fail(LE_EINVAL, "null argument");
+  if (M < 0) return fail(LE_EINVAL, "M < 0");
+  const int K = w->w.K;
+  if ((long long)M * K > LE_QGEMM_NOALLOC_MAX_ELEMS)
+    return fail(LE_EINVAL, "M*K = %lld exceeds the scratch limit of %d elements", (long long)M * K,
+                LE_QGEMM_NOALLOC_MAX_ELEMS);
+  std::lock_guard<std::mutex> lk(w->mu);
+  CK(cudaSetDevice(w->dev));
+  uint8_t* scratch = nullptr;
+  TRY(noalloc_scratch(w->dev, &scratch));
+  if (M == 0) return LE_OK;
+  cudaStream_t s = stream ? (cudaStream_t)stream : w->stream;
+  DevStatus* st = reinterpret_cast<DevStatus*>(scratch);
+  __half* x16 = reinterpret_cast<__half*>(scratch + 256);
+  CK(cudaMemsetAsync(st, 0, sizeof(DevStatus), s));
+  CK(launch_f32_to_f16(d_x, (long)M * K, x16, s));
+  EpiParams e{};
+  e.mode = EPI_F32;
+  e.M = M;
+  e.N = w->w.n_real;
+  e.out32 = d_y;
+  e.ldo = w->w.n_real;
+  CK(launch_gemm(w->w.qf, w->w.buf.as<uint8_t>(), w->w.n_real, K, x16, K, e, st, s));
+  DevStatus h{};
+  CK(cudaMemcpyAsync(&h, st, sizeof h, cudaMemcpyDeviceToHost, s));
+  CK(cudaStreamSynchronize(s));
+  if (h.code != DE_OK)
+    return fail(LE_EDEVICE, "kernel failure code %d at site %d (info %d)", h.code, h.where, h.info);
+  return LE_OK;
+}
+
 int le_info(char* buf, int len) {
   int n = 0, sms = 0;
   cudaDeviceProp p{};

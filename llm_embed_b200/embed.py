@@ -73,6 +73,7 @@ def lib() -> C.CDLL:
             L.le_qgemm.argtypes = [C.c_int, C.c_int, vp, C.c_int, C.c_int, fp, C.c_int, fp]
             L.le_qweight_create.argtypes = [C.c_int, C.c_int, vp, C.c_int, C.c_int, C.POINTER(vp)]
             L.le_qgemm_device.argtypes = [vp, vp, C.c_int, vp, vp]
+            L.le_qgemm_device_noalloc.argtypes = [vp, vp, C.c_int, vp, vp]
             L.le_qweight_free.argtypes = [vp]
             L.le_info.argtypes = [C.c_char_p, C.c_int]
             L.le_set_profiling.argtypes = [vp, C.c_int]
@@ -257,6 +258,15 @@ class QWeight:
 
     def matmul_device(self, d_x: int, M: int, d_y: int, stream: int = 0) -> None:
         _check(lib().le_qgemm_device(self._h, d_x, M, d_y, stream or None))
+
+    # Largest M*K le_qgemm_device_noalloc accepts (LE_QGEMM_NOALLOC_MAX_ELEMS).
+    NOALLOC_MAX_ELEMS = 4 * 1024 * 1024
+
+    def matmul_device_noalloc(self, d_x: int, M: int, d_y: int, stream: int = 0) -> None:
+        """matmul_device through the entry point that allocates nothing: it
+        uses a fixed per-device scratch array shared by all calls (M*K <=
+        NOALLOC_MAX_ELEMS) and waits for `stream` before returning."""
+        _check(lib().le_qgemm_device_noalloc(self._h, d_x, M, d_y, stream or None))
 
     def close(self):
         if self._h:
