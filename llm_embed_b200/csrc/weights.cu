@@ -8,7 +8,8 @@ namespace le {
 
 // One thread per (virtual row, 64-column k-step).  Virtual row v maps to a
 // source row: identity (src0), or for the merged FFN up/gate matrix, tile
-// t = v/256 holds up rows 128t..128t+127 then gate rows 128t..128t+127.
+// t = v/128 holds up rows 64t..64t+63 (src0) then gate rows 64t..64t+63
+// (src1).
 template <int TYPE>
 __global__ void repack_kernel(const uint8_t* __restrict__ src0, const uint8_t* __restrict__ src1, long src_row_bytes,
                               int N_src, int K, int n_tiles, int interleave, uint8_t* __restrict__ dst) {
