@@ -117,7 +117,8 @@ struct HostBuf {
 
 // A repacked projection weight.
 struct QMat {
-  DevBuf buf;
+  DevBuf buf;      // tile-blocked quantised weight (common.cuh)
+  DevBuf w16;      // its fp16 operand values [n_virt][K] for the large-batch GEMM
   int type = 0;   // GGML type
   int qf = 0;     // QFmt
   int n_real = 0;  // real output rows
@@ -252,6 +253,8 @@ static int make_qmat(QMat& q, int type, const void* src0, const void* src1, int 
   if (interleave) CK(cudaMemcpyAsync(raw.as<uint8_t>() + nb, src1, nb, cudaMemcpyHostToDevice, s));
   CK(launch_repack(type, raw.as<uint8_t>(), interleave ? raw.as<uint8_t>() + nb : nullptr, rb, N, K, n_tiles,
                    interleave ? 1 : 0, q.buf.as<uint8_t>(), s));
+  TRY(q.w16.ensure((size_t)q.n_virt * K * 2));
+  CK(launch_expand_f16(q.qf, q.buf.as<uint8_t>(), q.n_virt, K, q.w16.as<__half>(), s));
   CK(cudaStreamSynchronize(s));
   return LE_OK;
 }
@@ -297,7 +300,8 @@ static int ensure_ws(le_model* m, int tokens, int seqs) {
 
 static int gemm(le_model* m, int cls, const QMat& W, const __half* A, int lda, const EpiParams& ep, cudaStream_t s) {
   m->prof.begin(cls, s);
-  CK(launch_gemm(W.qf, W.buf.as<uint8_t>(), W.n_virt, W.K, A, lda, ep, m->status.as<DevStatus>(), s));
+  CK(launch_gemm(W.qf, W.buf.as<uint8_t>(), W.w16.as<__half>(), W.n_virt, W.K, A, lda, ep, m->status.as<DevStatus>(),
+                 s));
   m->prof.end(s);
   return LE_OK;
 }
@@ -864,7 +868,8 @@ int le_qgemm_device(le_qweight* w, const float* d_x, int M, float* d_y, void* st
   e.N = w->w.n_real;
   e.out32 = d_y;
   e.ldo = w->w.n_real;
-  CK(launch_gemm(w->w.qf, w->w.buf.as<uint8_t>(), w->w.n_real, K, w->x16.as<__half>(), K, e, w->status.as<DevStatus>(), s));
+  CK(launch_gemm(w->w.qf, w->w.buf.as<uint8_t>(), w->w.w16.as<__half>(), w->w.n_real, K, w->x16.as<__half>(), K, e,
+                 w->status.as<DevStatus>(), s));
   return LE_OK;
 }
 
@@ -940,7 +945,7 @@ int le_qgemm_device_noalloc(le_qweight* w, const float* d_x, int M, float* d_y, 
   e.N = w->w.n_real;
   e.out32 = d_y;
   e.ldo = w->w.n_real;
-  CK(launch_gemm(w->w.qf, w->w.buf.as<uint8_t>(), w->w.n_real, K, x16, K, e, st, s));
+  CK(launch_gemm(w->w.qf, w->w.buf.as<uint8_t>(), w->w.w16.as<__half>(), w->w.n_real, K, x16, K, e, st, s));
   DevStatus h{};
   CK(cudaMemcpyAsync(&h, st, sizeof h, cudaMemcpyDeviceToHost, s));
   CK(cudaStreamSynchronize(s));

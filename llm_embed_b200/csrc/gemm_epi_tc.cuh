@@ -1,0 +1,133 @@
+// Epilogue of the tensor-core GEMM kernels (gemm_tc2.cu, gemm_f16.cu): one
+// warp drains 32 accumulator rows (TMEM lanes 32*(warp%4) ..) of a
+// 256-column tile, applies the fused epilogue and writes 32-row x 128-byte
+// output blocks with TMA stores from 128B-swizzled staging buffers.
+#pragma once
+#include <cudaTypedefs.h>
+
+#include "epilogue.cuh"
+#include "tcgen05.cuh"
+
+namespace le {
+namespace tcx {
+
+// TMA store of a 32-row block from shared memory (bulk-group completion).
+__device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, uint32_t src, int c0, int c1) {
+  asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];" ::"l"(
+                   reinterpret_cast<uint64_t>(map)),
+               "r"(src), "r"(c0), "r"(c1)
+               : "memory");
+  asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+}
+
+// One warp stages its 32 rows x 128 bytes (words[32] per lane = its row) in
+// buffer `buf` of its two 4 KB buffers at `stage` and stores it with one TMA
+// store at (col0, row0).  Before a buffer is rewritten the store that last
+// read it must be done (at most one store group left in flight).
+__device__ __forceinline__ void emit_block(const CUtensorMap* map, uint32_t stage, int& buf, const uint32_t* words,
+                                           int col0, int row0) {
+  const int lane = threadIdx.x & 31;
+  if (lane == 0) asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory");
+  __syncwarp();
+  const uint32_t base = stage + buf * 4096 + lane * 128;
+#pragma unroll
+  for (int q = 0; q < 8; q++)
+    asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(base + ((q ^ (lane & 7)) << 4)), "r"(words[4 * q]),
+                 "r"(words[4 * q + 1]), "r"(words[4 * q + 2]), "r"(words[4 * q + 3])
+                 : "memory");
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+  __syncwarp();
+  if (lane == 0) tma_store_2d(map, stage + buf * 4096, col0, row0);
+  buf ^= 1;
+}
+
+// gelu(v) * u with the GeLU of ops_simd.go:27-43:
+//   t = 0.7978845608 v (1 + 0.044715 v^2)
+//   tanh_r(t) = t (27 + t^2) / (27 + 9 t^2), +-1 where |t| > 4.97
+//   gelu = 0.5 v (1 + tanh_r(t))
+// evaluated as t = v (0.7978845608 + 0.0356774081 v^2), tanh_r = t ((27 +
+// t^2) / (27 + 9 t^2)) with the fast reciprocal, and 0.5 v u + 0.5 v u
+// tanh_r; the product is rounded to fp16 (the next GEMM's operand), far
+// coarser than these few-ulp changes of the evaluation order.
+__device__ __forceinline__ float geglu(float v, float u) {
+  const float t = v * fmaf(0.0356774081f, v * v, 0.7978845608f);
+  const float t2 = t * t;
+  float th = t * __fdividef(27.0f + t2, fmaf(9.0f, t2, 27.0f));
+  th = t > 4.97f ? 1.0f : (t < -4.97f ? -1.0f : th);
+  const float hv = (0.5f * v) * u;
+  return fmaf(hv, th, hv);
+}
+
+// Epilogue of one 256-column pair tile for the calling warp: accumulator
+// columns [c_begin, c_end) of TMEM address `tbase` (its lane quarter already
+// added), output rows row0 .. row0+31, tile column origin n0 (virtual rows of
+// the weight).  Rows at or beyond ep.M are clipped by the TMA store.
+__device__ __forceinline__ void epilogue_tile(const EpiParams& ep, const CUtensorMap* tmap_out, uint32_t tbase,
+                                              int row0, int n0, int c_begin, int c_end, uint32_t stage, int& buf) {
+  const int lane = threadIdx.x & 31;
+  uint32_t words[32];
+  if (ep.mode == EPI_GEGLU) {
+    // Each 128-column half is one weight tile: up columns c, gate c + 64;
+    // its 64 outputs form one fp16 block.
+#pragma unroll 1
+    for (int c = c_begin; c < c_end; c += TILE_N) {
+#pragma unroll
+      for (int h = 0; h < 4; h++) {
+        float up[16], gt[16];
+        tmem_ld16(tbase + c + 16 * h, up);
+        tmem_ld16(tbase + c + 16 * h + GEGLU_HALF, gt);
+#pragma unroll
+        for (int i = 0; i < 8; i++)
+          words[8 * h + i] = pack_half2(geglu(gt[2 * i], up[2 * i]), geglu(gt[2 * i + 1], up[2 * i + 1]));
+      }
+      emit_block(tmap_out, stage, buf, words, (n0 + c) / TILE_N * GEGLU_HALF, row0);
+    }
+  } else if (ep.mode == EPI_QKV) {
+    // One head (64 columns) per fp16 block; RoPE on the Q and K heads
+    // (ops_simd.go:127-137), pairs (2i, 2i+1) rotated by the row's position.
+    const bool rope = n0 < ep.rope_cols;
+    const long prow = (long)ep.pos[min(row0 + lane, ep.M - 1)] * 32;
+#pragma unroll 1
+    for (int c = c_begin; c < c_end; c += 64) {
+#pragma unroll
+      for (int h = 0; h < 4; h++) {  // 16 columns = rotation pairs 8h .. 8h+7
+        float4 cq[2], sq[2];
+        if (rope) {
+          const float4* cp = reinterpret_cast<const float4*>(ep.rope_cos + prow + 8 * h);
+          const float4* sp = reinterpret_cast<const float4*>(ep.rope_sin + prow + 8 * h);
+          cq[0] = __ldg(cp);
+          cq[1] = __ldg(cp + 1);
+          sq[0] = __ldg(sp);
+          sq[1] = __ldg(sp + 1);
+        }
+        float v[16];
+        tmem_ld16(tbase + c + 16 * h, v);
+        if (rope) {
+          const float cc[8] = {cq[0].x, cq[0].y, cq[0].z, cq[0].w, cq[1].x, cq[1].y, cq[1].z, cq[1].w};
+          const float ss[8] = {sq[0].x, sq[0].y, sq[0].z, sq[0].w, sq[1].x, sq[1].y, sq[1].z, sq[1].w};
+#pragma unroll
+          for (int i = 0; i < 8; i++) {
+            const float x0 = v[2 * i], x1 = v[2 * i + 1];
+            v[2 * i] = __fsub_rn(__fmul_rn(x0, cc[i]), __fmul_rn(x1, ss[i]));
+            v[2 * i + 1] = __fadd_rn(__fmul_rn(x0, ss[i]), __fmul_rn(x1, cc[i]));
+          }
+        }
+#pragma unroll
+        for (int i = 0; i < 8; i++) words[8 * h + i] = pack_half2(v[2 * i], v[2 * i + 1]);
+      }
+      emit_block(tmap_out, stage, buf, words, n0 + c, row0);
+    }
+  } else {
+#pragma unroll 1
+    for (int c = c_begin; c < c_end; c += 32) {
+      float v[32];
+      tmem_ld32(tbase + c, v);
+#pragma unroll
+      for (int i = 0; i < 32; i++) words[i] = __float_as_uint(v[i]);
+      emit_block(tmap_out, stage, buf, words, n0 + c, row0);
+    }
+  }
+}
+
+}  // namespace tcx
+}  // namespace le

@@ -35,6 +35,7 @@
 
 #include <mutex>
 
+#include "gemm_epi_tc.cuh"
 #include "kernels.h"
 #include "tcgen05.cuh"
 
@@ -95,35 +96,6 @@ struct Layout {
   static constexpr int ALLOC = BYTES + 1024;
   static_assert(ALLOC <= 232448, "shared memory budget of one CTA exceeded");
 };
-
-// TMA store of a 32-row block from shared memory (bulk-group completion).
-__device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, uint32_t src, int c0, int c1) {
-  asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];" ::"l"(
-                   reinterpret_cast<uint64_t>(map)),
-               "r"(src), "r"(c0), "r"(c1)
-               : "memory");
-  asm volatile("cp.async.bulk.commit_group;" ::: "memory");
-}
-
-// One warp stages its 32 rows x 128 bytes (words[32] per lane = its row) in
-// buffer `buf` and stores it with one TMA store at (col0, row0).  Buffers
-// alternate; before reuse the store that last read a buffer must be done.
-__device__ __forceinline__ void emit_block(const CUtensorMap* map, uint32_t stage, int& buf, const uint32_t* words,
-                                           int col0, int row0) {
-  const int lane = threadIdx.x & 31;
-  if (lane == 0) asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory");
-  __syncwarp();
-  const uint32_t base = stage + buf * 4096 + lane * 128;
-#pragma unroll
-  for (int q = 0; q < 8; q++)
-    asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(base + ((q ^ (lane & 7)) << 4)), "r"(words[4 * q]),
-                 "r"(words[4 * q + 1]), "r"(words[4 * q + 2]), "r"(words[4 * q + 3])
-                 : "memory");
-  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-  __syncwarp();
-  if (lane == 0) tma_store_2d(map, stage + buf * 4096, col0, row0);
-  buf ^= 1;
-}
 
 template <int QF>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NTHREADS, 1)
@@ -317,66 +289,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NTHREADS, 1)
       const int mt = tile / n_tiles, nt = tile % n_tiles;
       const int row0 = mt * PM + rank * UM + quarter * 32;
       const uint32_t tbase = tmem + acc * PN + ((uint32_t)(quarter * 32) << 16);
-      if (row0 < ep.M) {  // warp-uniform
-        uint32_t words[32];
-        if (ep.mode == EPI_GEGLU) {
-          // Each 128-column half is one weight tile: up columns c, gate
-          // c + 64; its 64 outputs form one fp16 block.
-#pragma unroll 1
-          for (int c = c_begin; c < c_end; c += TILE_N) {
-#pragma unroll
-            for (int h = 0; h < 4; h++) {
-              float up[16], gt[16];
-              tmem_ld16(tbase + c + 16 * h, up);
-              tmem_ld16(tbase + c + 16 * h + GEGLU_HALF, gt);
-#pragma unroll
-              for (int i = 0; i < 8; i++)
-                words[8 * h + i] = pack_half2(gelu_tanh_rational(gt[2 * i]) * up[2 * i],
-                                              gelu_tanh_rational(gt[2 * i + 1]) * up[2 * i + 1]);
-            }
-            emit_block(&tmap_out, stage, buf, words, (nt * PN + c) / TILE_N * GEGLU_HALF, row0);
-          }
-        } else if (ep.mode == EPI_QKV) {
-          // One head (64 columns) per fp16 block; RoPE on Q and K heads.
-          const bool rope = nt * PN < ep.rope_cols;
-          const long prow = (long)ep.pos[min(row0 + lane, ep.M - 1)] * 32;
-#pragma unroll 1
-          for (int c = c_begin; c < c_end; c += 64) {
-#pragma unroll
-            for (int h = 0; h < 2; h++) {
-              float v[32];
-              tmem_ld32(tbase + c + 32 * h, v);
-              if (rope) {
-                const float4* cp = reinterpret_cast<const float4*>(ep.rope_cos + prow + 16 * h);
-                const float4* sp = reinterpret_cast<const float4*>(ep.rope_sin + prow + 16 * h);
-#pragma unroll
-                for (int q = 0; q < 4; q++) {
-                  const float4 a = cp[q], b = sp[q];
-                  const float cc[4] = {a.x, a.y, a.z, a.w}, ss[4] = {b.x, b.y, b.z, b.w};
-#pragma unroll
-                  for (int i = 0; i < 4; i++) {
-                    const float x0 = v[8 * q + 2 * i], x1 = v[8 * q + 2 * i + 1];
-                    v[8 * q + 2 * i] = __fsub_rn(__fmul_rn(x0, cc[i]), __fmul_rn(x1, ss[i]));
-                    v[8 * q + 2 * i + 1] = __fadd_rn(__fmul_rn(x0, ss[i]), __fmul_rn(x1, cc[i]));
-                  }
-                }
-              }
-#pragma unroll
-              for (int i = 0; i < 16; i++) words[16 * h + i] = pack_half2(v[2 * i], v[2 * i + 1]);
-            }
-            emit_block(&tmap_out, stage, buf, words, nt * PN + c, row0);
-          }
-        } else {
-#pragma unroll 1
-          for (int c = c_begin; c < c_end; c += 32) {
-            float v[32];
-            tmem_ld32(tbase + c, v);
-#pragma unroll
-            for (int i = 0; i < 32; i++) words[i] = __float_as_uint(v[i]);
-            emit_block(&tmap_out, stage, buf, words, nt * PN + c, row0);
-          }
-        }
-      }
+      if (row0 < ep.M)  // warp-uniform
+        epilogue_tile(ep, &tmap_out, tbase, row0, nt * PN, c_begin, c_end, stage, buf);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive_cluster(tempty_leader0 + 8 * acc);

@@ -14,6 +14,7 @@ cudaError_t launch_repack(int type, const uint8_t* src0, const uint8_t* src1, lo
                           int n_tiles, int interleave, uint8_t* dst, cudaStream_t s);
 cudaError_t launch_dequant_tiles(int qf, const uint8_t* w, int n_rows, int K, int mode, float* out, cudaStream_t s);
 cudaError_t launch_gguf_rows(int type, const uint8_t* src, long row_bytes, int n_rows, int K, float* out, cudaStream_t s);
+cudaError_t launch_expand_f16(int qf, const uint8_t* w, int n_rows, int K, __half* out, cudaStream_t s);
 
 // elementwise.cu
 cudaError_t launch_embed_ln(const int32_t* ids, int emb_type, const uint8_t* emb, long emb_row_bytes, int vocab,
@@ -37,5 +38,9 @@ cudaError_t launch_gemm_simt(int qf, const uint8_t* W, int n_virtual, int K, con
 // gemm_tc2.cu
 cudaError_t launch_gemm_tc2(int qf, const uint8_t* W, int n_virtual, int K, const __half* A, long lda,
                             const EpiParams& ep, DevStatus* status, cudaStream_t s);
+
+// gemm_f16.cu
+cudaError_t launch_gemm_f16(const __half* W16, int n_virtual, int K, const __half* A, long lda, const EpiParams& ep,
+                            DevStatus* status, cudaStream_t s);
 
 }  // namespace le

@@ -106,6 +106,23 @@ __global__ void dequant_tiles_kernel(const uint8_t* __restrict__ w, int n_rows, 
   }
 }
 
+// fp16 tensor-core operands of the tile layout as a row-major [n_rows][K]
+// fp16 matrix (virtual row order), the B operand of the large-batch GEMM:
+// the same dq8_f16 values the in-shared-memory dequant produces.
+template <int QF>
+__global__ void expand_f16_kernel(const uint8_t* __restrict__ w, int n_rows, int K, __half* __restrict__ out) {
+  const int ksteps = K / TILE_K;
+  const long idx = (long)blockIdx.x * blockDim.x + threadIdx.x;  // (row, k-step, group)
+  if (idx >= (long)n_rows * ksteps * 8) return;
+  const int g = (int)(idx & 7);
+  const int ks = (int)((idx >> 3) % ksteps);
+  const int v = (int)((idx >> 3) / ksteps);
+  const int t = v / TILE_N, r = v % TILE_N;
+  const uint8_t* chunk = w + ((long)t * ksteps + ks) * chunk_bytes(QF);
+  const uint2 u = *reinterpret_cast<const uint2*>(chunk + r * TILE_K + g * 8);
+  *reinterpret_cast<uint4*>(out + (long)v * K + ks * TILE_K + g * 8) = dq8_f16<QF>(u, chunk + TILE_Q_BYTES, r, g);
+}
+
 // Dequantise whole GGUF rows (used for the embedding table check).
 __global__ void gguf_rows_kernel(int type, const uint8_t* __restrict__ src, long row_bytes, int n_rows, int K,
                                  float* __restrict__ out) {
@@ -147,6 +164,19 @@ cudaError_t launch_dequant_tiles(int qf, const uint8_t* w, int n_rows, int K, in
 cudaError_t launch_gguf_rows(int type, const uint8_t* src, long row_bytes, int n_rows, int K, float* out, cudaStream_t s) {
   const long n = (long)n_rows * K;
   gguf_rows_kernel<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(type, src, row_bytes, n_rows, K, out);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_expand_f16(int qf, const uint8_t* w, int n_rows, int K, __half* out, cudaStream_t s) {
+  const long n = (long)n_rows * (K / TILE_K) * 8;
+  const int bs = 256;
+  const unsigned grid = (unsigned)((n + bs - 1) / bs);
+  switch (qf) {
+    case QF_Q8_0: expand_f16_kernel<QF_Q8_0><<<grid, bs, 0, s>>>(w, n_rows, K, out); break;
+    case QF_KMIN: expand_f16_kernel<QF_KMIN><<<grid, bs, 0, s>>>(w, n_rows, K, out); break;
+    case QF_Q6K: expand_f16_kernel<QF_Q6K><<<grid, bs, 0, s>>>(w, n_rows, K, out); break;
+    default: return cudaErrorInvalidValue;
+  }
   return cudaGetLastError();
 }
 

@@ -329,6 +329,33 @@ def test_qgemm_full_size_vs_torch():
     assert cos.min().item() >= COS_MIN
 
 
+@pytest.mark.parametrize("qtype", [synth.GGML_Q8_0, synth.GGML_Q4_K, synth.GGML_Q6_K])
+def test_gemm_paths_bitwise_equal(qtype):
+    """The large-batch kernel (fp16 weights via TMA, M >= 256) and the
+    in-shared-memory dequant kernel (64 <= M < 256) use the same fp16 operand
+    values and MMA order: rows of an M=256 call equal the same rows computed
+    at M=255 and M=64, bit for bit."""
+    import torch
+    K, N = 768, 2304
+    rng = np.random.default_rng([7, qtype])
+    w = rng.standard_normal((N, K), dtype=np.float32) * np.float32(0.02)
+    qw = QWeight(qtype, synth.quantize(w, qtype), N, K)
+    try:
+        x = torch.randn(256, K, device="cuda", generator=torch.Generator("cuda").manual_seed(3))
+        outs = {}
+        for M in (256, 255, 64):
+            y = torch.empty(M, N, device="cuda")
+            torch.cuda.synchronize()
+            qw.matmul_device(x.data_ptr(), M, y.data_ptr())
+            torch.cuda.synchronize()
+            outs[M] = y
+        assert torch.isfinite(outs[256]).all()
+        assert torch.equal(outs[256][:255].view(torch.int32), outs[255].view(torch.int32))
+        assert torch.equal(outs[256][:64].view(torch.int32), outs[64].view(torch.int32))
+    finally:
+        qw.close()
+
+
 def test_config2_full_batch_properties(model_path):
     """The full configs[2] batch (256 sequences): unit norms, run-to-run
     bit-identical, and oracle parity of a sample of its sequences."""
