@@ -62,8 +62,32 @@ __device__ __forceinline__ float geglu(float v, float u) {
 // columns [c_begin, c_end) of TMEM address `tbase` (its lane quarter already
 // added), output rows row0 .. row0+31, tile column origin n0 (virtual rows of
 // the weight).  Rows at or beyond ep.M are clipped by the TMA store.
+// RoPE of this lane's row: cos and sin of rotation pairs 0..31, loaded before
+// the accumulator is ready (rope_prefetch) so their latency overlaps the MMA.
+struct RopeRow {
+  float4 c[8], s[8];
+};
+
+__device__ __forceinline__ bool rope_tile(const EpiParams& ep, int n0) { return ep.mode == EPI_QKV && n0 < ep.rope_cols; }
+
+__device__ __forceinline__ void rope_prefetch(const EpiParams& ep, int row0, RopeRow& rr) {
+  const int lane = threadIdx.x & 31;
+  const long prow = (long)ep.pos[min(row0 + lane, ep.M - 1)] * 32;
+  const float4* cp = reinterpret_cast<const float4*>(ep.rope_cos + prow);
+  const float4* sp = reinterpret_cast<const float4*>(ep.rope_sin + prow);
+#pragma unroll
+  for (int q = 0; q < 8; q++) {
+    rr.c[q] = __ldg(cp + q);
+    rr.s[q] = __ldg(sp + q);
+  }
+}
+
+// PRE: the caller passes the row's RoPE values (rope_prefetch) in `pre`;
+// otherwise they are loaded here, per 16 columns.
+template <bool PRE = false>
 __device__ __forceinline__ void epilogue_tile(const EpiParams& ep, const CUtensorMap* tmap_out, uint32_t tbase,
-                                              int row0, int n0, int c_begin, int c_end, uint32_t stage, int& buf) {
+                                              int row0, int n0, int c_begin, int c_end, uint32_t stage, int& buf,
+                                              const RopeRow* pre = nullptr) {
   const int lane = threadIdx.x & 31;
   uint32_t words[32];
   if (ep.mode == EPI_GEGLU) {
@@ -86,13 +110,18 @@ __device__ __forceinline__ void epilogue_tile(const EpiParams& ep, const CUtenso
     // One head (64 columns) per fp16 block; RoPE on the Q and K heads
     // (ops_simd.go:127-137), pairs (2i, 2i+1) rotated by the row's position.
     const bool rope = n0 < ep.rope_cols;
-    const long prow = (long)ep.pos[min(row0 + lane, ep.M - 1)] * 32;
+    const long prow = PRE ? 0 : (long)ep.pos[min(row0 + lane, ep.M - 1)] * 32;
 #pragma unroll 1
     for (int c = c_begin; c < c_end; c += 64) {
 #pragma unroll
       for (int h = 0; h < 4; h++) {  // 16 columns = rotation pairs 8h .. 8h+7
         float4 cq[2], sq[2];
-        if (rope) {
+        if constexpr (PRE) {
+          cq[0] = pre->c[2 * h];
+          cq[1] = pre->c[2 * h + 1];
+          sq[0] = pre->s[2 * h];
+          sq[1] = pre->s[2 * h + 1];
+        } else if (rope) {
           const float4* cp = reinterpret_cast<const float4*>(ep.rope_cos + prow + 8 * h);
           const float4* sp = reinterpret_cast<const float4*>(ep.rope_sin + prow + 8 * h);
           cq[0] = __ldg(cp);

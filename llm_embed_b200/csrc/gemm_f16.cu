@@ -97,6 +97,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NTHREADS, 1)
   const int ksteps = K / BK;
   const int total = m_tiles * n_tiles;
   const int cluster = blockIdx.x >> 1, nclusters = gridDim.x >> 1;
+#ifdef LE_TC_WAITPROF
+  const long long t_kernel0 = clock64();
+#endif
 
   if (threadIdx.x == 0) {
     *abort_flag = 0;
@@ -184,14 +187,17 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NTHREADS, 1)
     int tcount = 0;
     for (int tile = cluster; tile < total; tile += nclusters, tcount++) {
       const int acc = tcount & 1;
+      const int mt = tile / n_tiles, nt = tile % n_tiles;
+      const int row0 = mt * PM + rank * UM + quarter * 32;
+      RopeRow rr;
+      const bool rope = row0 < ep.M && rope_tile(ep, nt * PN);
+      if (rope) rope_prefetch(ep, row0, rr);
       const bool w = mbar_wait(tfull(acc), (tcount >> 1) & 1, abort_flag, status, 24);
       if (!__all_sync(0xffffffffu, w)) break;  // warp-uniform: tcgen05.ld is .sync.aligned
       tc_fence_after();
-      const int mt = tile / n_tiles, nt = tile % n_tiles;
-      const int row0 = mt * PM + rank * UM + quarter * 32;
       const uint32_t tbase = tmem + acc * PN + ((uint32_t)(quarter * 32) << 16);
       if (row0 < ep.M)  // warp-uniform
-        epilogue_tile(ep, &tmap_out, tbase, row0, nt * PN, c_begin, c_end, stage, buf);
+        epilogue_tile<true>(ep, &tmap_out, tbase, row0, nt * PN, c_begin, c_end, stage, buf, &rr);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive_cluster(tempty_leader0 + 8 * acc);
@@ -207,6 +213,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NTHREADS, 1)
     tc_fence_after();
     asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(TMEM_COLS));
   }
+#ifdef LE_TC_WAITPROF
+  if (threadIdx.x == 0) atomicAdd(&g_waitprof[0], (unsigned long long)(clock64() - t_kernel0));
+#endif
 }
 
 // ---------------------------------------------------------------- host ----
@@ -299,6 +308,17 @@ static cudaError_t launch(const __half* W16, int n_virtual, int K, const __half*
 }
 
 }  // namespace tcf
+
+#ifdef LE_TC_WAITPROF
+extern "C" int le_debug_waitprof3(unsigned long long* out, int reset) {
+  if (cudaMemcpyFromSymbol(out, tcx::g_waitprof, sizeof(tcx::g_waitprof)) != cudaSuccess) return -2;
+  if (reset) {
+    unsigned long long z[10] = {};
+    if (cudaMemcpyToSymbol(tcx::g_waitprof, z, sizeof(z)) != cudaSuccess) return -2;
+  }
+  return 0;
+}
+#endif
 
 cudaError_t launch_gemm_f16(const __half* W16, int n_virtual, int K, const __half* A, long lda, const EpiParams& ep,
                             DevStatus* status, cudaStream_t s) {
