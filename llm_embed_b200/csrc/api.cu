@@ -185,6 +185,23 @@ struct Profiler {
   }
 };
 
+// An instantiated CUDA graph of forward() for one call shape.  Kernel
+// parameters hold the caller's id/offset/output pointers and the workspace
+// buffers, so those are part of the key; workspace growth drops all graphs.
+struct GraphEntry {
+  int T = 0, nseq = 0, max_len = 0, out_dim = 0;
+  const void* ids = nullptr;
+  const void* offsets = nullptr;
+  void* out = nullptr;
+  cudaGraphExec_t exec = nullptr;
+  uint64_t last_use = 0;
+};
+
+// Calls of at most this many tokens replay a cached graph of the forward
+// pass (launch overhead dominates them); larger ones launch directly.
+constexpr int GRAPH_MAX_TOKENS = 4096;
+constexpr size_t GRAPH_CACHE = 32;
+
 struct le_model {
   int dev = 0;
   Profiler prof;
@@ -196,9 +213,19 @@ struct le_model {
   DevBuf emb, type0, embd_w, embd_b, rope_cos, rope_sin, status;
   std::vector<Layer> layers;
   cudaStream_t stream = nullptr;
+  cudaStream_t capture_stream = nullptr;  // graphs are captured here, replayed on the caller's stream
+  std::vector<GraphEntry> graphs;
+  uint64_t graph_clock = 0;
   std::mutex mu;
   Workspace ws;
+  void drop_graphs() {
+    for (auto& g : graphs)
+      if (g.exec) cudaGraphExecDestroy(g.exec);
+    graphs.clear();
+  }
   ~le_model() {
+    drop_graphs();
+    if (capture_stream) cudaStreamDestroy(capture_stream);
     if (stream) cudaStreamDestroy(stream);
   }
 };
@@ -272,6 +299,7 @@ static int upload_f32(DevBuf& b, const le_tensor_desc* t, int n, cudaStream_t s)
 static int ensure_ws(le_model* m, int tokens, int seqs) {
   Workspace& w = m->ws;
   const int H = m->hp.hidden, F = m->hp.ffn;
+  if (tokens > w.cap_tokens || seqs > w.cap_seqs) m->drop_graphs();  // they point at the old buffers
   if (tokens > w.cap_tokens) {
     const size_t T = (size_t)std::max(tokens, 256);
     TRY(w.ids.ensure(T * 4));
@@ -369,6 +397,55 @@ static int forward(le_model* m, const int32_t* d_ids, const int32_t* d_offsets, 
   return LE_OK;
 }
 
+// forward() through the graph cache: a call shape seen before replays its
+// graph with one launch; a new small shape runs directly and is captured
+// (on the model's capture stream, which executes nothing) for next time.
+static int run_forward(le_model* m, const int32_t* d_ids, const int32_t* d_offsets, int nseq, int T, int max_len,
+                       int out_dim, float* d_out, cudaStream_t s) {
+  if (m->prof.on || T <= 0 || T > GRAPH_MAX_TOKENS)
+    return forward(m, d_ids, d_offsets, nseq, T, max_len, out_dim, d_out, s);
+  for (auto& g : m->graphs)
+    if (g.T == T && g.nseq == nseq && g.max_len == max_len && g.out_dim == out_dim && g.ids == d_ids &&
+        g.offsets == d_offsets && g.out == d_out) {
+      g.last_use = ++m->graph_clock;
+      CK(cudaGraphLaunch(g.exec, s));
+      return LE_OK;
+    }
+  TRY(forward(m, d_ids, d_offsets, nseq, T, max_len, out_dim, d_out, s));
+  cudaGraph_t graph = nullptr;
+  CK(cudaStreamBeginCapture(m->capture_stream, cudaStreamCaptureModeThreadLocal));
+  const int rc = forward(m, d_ids, d_offsets, nseq, T, max_len, out_dim, d_out, m->capture_stream);
+  const cudaError_t ce = cudaStreamEndCapture(m->capture_stream, &graph);
+  if (rc != LE_OK || ce != cudaSuccess) {
+    if (graph) cudaGraphDestroy(graph);
+    cudaGetLastError();
+    return rc != LE_OK ? rc : LE_OK;  // the direct run above produced the result
+  }
+  GraphEntry e;
+  const cudaError_t ie = cudaGraphInstantiate(&e.exec, graph, 0);
+  cudaGraphDestroy(graph);
+  if (ie != cudaSuccess) {
+    cudaGetLastError();
+    return LE_OK;
+  }
+  if (m->graphs.size() >= GRAPH_CACHE) {
+    auto lru = std::min_element(m->graphs.begin(), m->graphs.end(),
+                                [](const GraphEntry& a, const GraphEntry& b) { return a.last_use < b.last_use; });
+    cudaGraphExecDestroy(lru->exec);
+    m->graphs.erase(lru);
+  }
+  e.T = T;
+  e.nseq = nseq;
+  e.max_len = max_len;
+  e.out_dim = out_dim;
+  e.ids = d_ids;
+  e.offsets = d_offsets;
+  e.out = d_out;
+  e.last_use = ++m->graph_clock;
+  m->graphs.push_back(e);
+  return LE_OK;
+}
+
 // One device's share: chunks of whole sequences of at most CHUNK_TOKENS.
 static int embed_host(le_model* m, const int32_t* ids, const int32_t* offs, int nseq, int out_dim, float* out) {
   std::lock_guard<std::mutex> lk(m->mu);
@@ -390,7 +467,7 @@ static int embed_host(le_model* m, const int32_t* ids, const int32_t* offs, int 
     for (int i = 0; i <= n; i++) ho[i] = offs[s0 + i] - offs[s0];
     CK(cudaMemcpyAsync(w.ids.p, hi, (size_t)T * 4, cudaMemcpyHostToDevice, s));
     CK(cudaMemcpyAsync(w.offsets.p, ho, (size_t)(n + 1) * 4, cudaMemcpyHostToDevice, s));
-    TRY(forward(m, w.ids.as<int32_t>(), w.offsets.as<int32_t>(), n, T, maxlen, out_dim, w.out.as<float>(), s));
+    TRY(run_forward(m, w.ids.as<int32_t>(), w.offsets.as<int32_t>(), n, T, maxlen, out_dim, w.out.as<float>(), s));
     CK(cudaMemcpyAsync(w.h_out.p, w.out.p, (size_t)n * out_dim * 4, cudaMemcpyDeviceToHost, s));
     TRY(check_status(m->status, s));
     std::memcpy(out + (size_t)s0 * out_dim, w.h_out.p, (size_t)n * out_dim * 4);
@@ -571,6 +648,7 @@ static int load_impl(int dev, const le_tensor_desc* ts, int nt, const le_hparams
   m->hp = *hp;
   m->head_dim = hp->hidden / hp->heads;
   CK(cudaStreamCreateWithFlags(&m->stream, cudaStreamNonBlocking));
+  CK(cudaStreamCreateWithFlags(&m->capture_stream, cudaStreamNonBlocking));
   cudaStream_t s = m->stream;
   const int H = hp->hidden, F = hp->ffn;
   auto need = [&](const std::string& n) { return find(ts, nt, n); };
@@ -771,7 +849,7 @@ int le_embed_ids_device(le_model* m, const int32_t* d_ids, const int32_t* d_offs
   CK(cudaSetDevice(m->dev));
   cudaStream_t s = stream ? (cudaStream_t)stream : m->stream;
   TRY(ensure_ws(m, n_tokens, nseq));
-  return forward(m, d_ids, d_offsets, nseq, n_tokens, max_len, out_dim, d_out, s);
+  return run_forward(m, d_ids, d_offsets, nseq, n_tokens, max_len, out_dim, d_out, s);
 }
 
 int le_sync(le_model* m) {

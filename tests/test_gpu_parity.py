@@ -199,6 +199,31 @@ def test_batch_equals_single_bitwise(model_path):
         e.Close()
 
 
+def test_graph_replay_matches_direct(model_path):
+    """Small calls replay a captured CUDA graph after their first (direct)
+    run: repeated calls, and device calls with other output pointers, give
+    the same bits as the first call."""
+    import torch
+    e = Embedder.Load(model_path(small_spec()))
+    try:
+        ids, offs = synth.make_ids([5, 9, 3], seed=4, vocab=2048)
+        first = e.EmbedIDs(ids, offs)
+        for _ in range(3):
+            assert np.array_equal(e.EmbedIDs(ids, offs).view(np.uint32), first.view(np.uint32))
+        d_ids = torch.from_numpy(ids).cuda()
+        d_offs = torch.from_numpy(offs).cuda()
+        outs = [torch.zeros(3, 768, device="cuda") for _ in range(2)]
+        torch.cuda.synchronize()  # the model's stream does not order with torch's
+        for _ in range(2):
+            for o in outs:
+                e.embed_device(d_ids.data_ptr(), d_offs.data_ptr(), 3, int(offs[-1]), 9, o.data_ptr(), 0)
+        e.sync()
+        for o in outs:
+            assert np.array_equal(o.cpu().numpy().view(np.uint32), first.view(np.uint32))
+    finally:
+        e.Close()
+
+
 def test_concurrent_calls(model_path):
     """16 threads x 3 calls on one model give the single-thread results
     (embedder_test.go:255-305)."""
