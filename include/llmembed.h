@@ -150,8 +150,9 @@ int le_qgemm_device_noalloc(le_qweight* w, const float* d_x, int M, float* d_y, 
  * counts every kernel this library launched for the model (profiling on or
  * off).  Classes: 0 QKV GEMM, 1 attention-output GEMM, 2 FFN up/gate GEMM,
  * 3 FFN down GEMM, 4 attention, 5 LayerNorm, 6 embedding gather + LN,
- * 7 positions + mean-pool. */
-#define LE_NCLASS 8
+ * 7 positions + mean-pool, 8 the single-kernel forward of small calls
+ * (<= 16 tokens; all layers in one launch). */
+#define LE_NCLASS 9
 typedef struct {
   int64_t launches;
   int64_t count[LE_NCLASS];

@@ -211,6 +211,8 @@ struct le_model {
   long emb_row_bytes = 0;
   int vocab = 0;
   DevBuf emb, type0, embd_w, embd_b, rope_cos, rope_sin, status;
+  DevBuf barrier;  // arrival counter of the single-kernel small forward
+  int sms = 0;
   std::vector<Layer> layers;
   cudaStream_t stream = nullptr;
   cudaStream_t capture_stream = nullptr;  // graphs are captured here, replayed on the caller's stream
@@ -355,6 +357,49 @@ static int forward(le_model* m, const int32_t* d_ids, const int32_t* d_offsets, 
   __half* att = w.att.as<__half>();
   __half* ff = w.ff.as<__half>();
   int32_t* pos = w.pos.as<int32_t>();
+  if (T > 0 && T <= SMALL_MAX_TOKENS && (int)m->layers.size() <= SMALL_MAX_LAYERS) {
+    // A few tokens: the whole encoder in one cooperative kernel, then the pool.
+    SmallParams sp{};
+    sp.T = T;
+    sp.nseq = nseq;
+    sp.n_layers = (int)m->layers.size();
+    sp.ids = d_ids;
+    sp.offsets = d_offsets;
+    sp.emb_type = m->emb_type;
+    sp.emb = m->emb.as<uint8_t>();
+    sp.emb_row_bytes = m->emb_row_bytes;
+    sp.vocab = m->vocab;
+    sp.type0 = m->type0.as<float>();
+    sp.embd_w = m->embd_w.as<float>();
+    sp.embd_b = m->embd_b.as<float>();
+    sp.eps = m->hp.ln_eps;
+    sp.rope_cos = m->rope_cos.as<float>();
+    sp.rope_sin = m->rope_sin.as<float>();
+    sp.pos = pos;
+    sp.qkv = qkv;
+    sp.att = att;
+    sp.y = y32;
+    sp.ff = ff;
+    sp.h_out = h32;
+    sp.barrier = m->barrier.as<unsigned>();
+    sp.status = m->status.as<DevStatus>();
+    for (int l = 0; l < sp.n_layers; l++) {
+      const Layer& L = m->layers[l];
+      const QMat* q[4] = {&L.qkv, &L.out, &L.upgate, &L.down};
+      const int modes[4] = {EPI_QKV, EPI_F32, EPI_GEGLU, EPI_F32};
+      for (int i = 0; i < 4; i++)
+        sp.layers[l].g[i] = SmallGemm{q[i]->buf.as<uint8_t>(), q[i]->qf, q[i]->K, q[i]->n_virt / 2, modes[i]};
+      sp.layers[l].attn_w = L.attn_w.as<float>();
+      sp.layers[l].attn_b = L.attn_b.as<float>();
+      sp.layers[l].out_w = L.out_w.as<float>();
+      sp.layers[l].out_b = L.out_b.as<float>();
+    }
+    if (small_forward_supported(sp, H, F, m->hp.heads, m->sms)) {
+      PLAUNCH(8, launch_forward_small(sp, s));
+      PLAUNCH(7, launch_pool(h32, d_offsets, nseq, H, out_dim, d_out, s));
+      return LE_OK;
+    }
+  }
   if (T > 0) {
     PLAUNCH(7, launch_positions(d_offsets, nseq, pos, s));
     PLAUNCH(6, launch_embed_ln(d_ids, m->emb_type, m->emb.as<uint8_t>(), m->emb_row_bytes, m->vocab,
@@ -649,6 +694,8 @@ static int load_impl(int dev, const le_tensor_desc* ts, int nt, const le_hparams
   m->head_dim = hp->hidden / hp->heads;
   CK(cudaStreamCreateWithFlags(&m->stream, cudaStreamNonBlocking));
   CK(cudaStreamCreateWithFlags(&m->capture_stream, cudaStreamNonBlocking));
+  CK(cudaDeviceGetAttribute(&m->sms, cudaDevAttrMultiProcessorCount, dev));
+  TRY(m->barrier.ensure(16));
   cudaStream_t s = m->stream;
   const int H = hp->hidden, F = hp->ffn;
   auto need = [&](const std::string& n) { return find(ts, nt, n); };

@@ -20,6 +20,7 @@
 
 #include <mutex>
 
+#include "attention_tile.cuh"
 #include "common.cuh"
 #include "kernels.h"
 
@@ -27,31 +28,13 @@ namespace le {
 
 namespace {
 
-constexpr int HD = 64;   // head dim
-constexpr int LDS = 72;  // smem row stride (halves): 144 B keeps ldmatrix rows on distinct banks
+using namespace attn;
+
 constexpr int SH_MAXL = 128;
 constexpr int SH_QROWS = 64;
 constexpr int SH_WARPS = SH_QROWS / 16;
 constexpr int SH_SMEM = (SH_QROWS + 2 * SH_MAXL) * LDS * 2;
 constexpr int QB = 64, KB = 64;  // long kernel blocks
-
-__device__ __forceinline__ void mma16816(float* c, const uint32_t* a, uint32_t b0, uint32_t b1) {
-  asm volatile(
-      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
-      "{%0,%1,%2,%3};\n"
-      : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
-      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
-}
-__device__ __forceinline__ void ldsm_x4(uint32_t* r, const __half* p) {
-  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
-               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
-               : "r"((uint32_t)__cvta_generic_to_shared(p)));
-}
-__device__ __forceinline__ void ldsm_x4_t(uint32_t* r, const __half* p) {
-  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
-               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
-               : "r"((uint32_t)__cvta_generic_to_shared(p)));
-}
 
 // Rows [r0, r0 + n) of one head's 64 columns into dst (zero rows past
 // `valid`), by all threads of the block.
@@ -77,53 +60,6 @@ __device__ __forceinline__ void load_rows_async(__half (*dst)[LDS], const __half
   }
 }
 
-// A fragments of 16 query rows (row0..row0+15) x 64 dims.
-__device__ __forceinline__ void load_q_frags(uint32_t (*qa)[4], __half (*sQ)[LDS], int row0) {
-  const int lane = threadIdx.x & 31;
-#pragma unroll
-  for (int kc = 0; kc < 4; kc++) ldsm_x4(qa[kc], &sQ[row0 + (lane & 15)][kc * 16 + (lane >> 4) * 8]);
-}
-
-// s += Q(16 x 64) . K(8 keys x 64)^T for keys key0..key0+7.
-__device__ __forceinline__ void qk_tile(float* s, uint32_t (*qa)[4], __half (*sK)[LDS], int key0) {
-  const int lane = threadIdx.x & 31;
-  uint32_t b[8];
-  ldsm_x4(b, &sK[key0 + (lane & 7)][(lane >> 3) * 8]);
-  ldsm_x4(b + 4, &sK[key0 + (lane & 7)][32 + (lane >> 3) * 8]);
-  mma16816(s, qa[0], b[0], b[1]);
-  mma16816(s, qa[1], b[2], b[3]);
-  mma16816(s, qa[2], b[4], b[5]);
-  mma16816(s, qa[3], b[6], b[7]);
-}
-
-// o[8][4] += P(16 x 16 keys) . V(16 keys x 64) for keys key0..key0+15.
-__device__ __forceinline__ void pv_chunk(float (*o)[4], const uint32_t* pa, __half (*sV)[LDS], int key0) {
-  const int lane = threadIdx.x & 31;
-#pragma unroll
-  for (int dt = 0; dt < 8; dt += 2) {
-    uint32_t b[4];
-    ldsm_x4_t(b, &sV[key0 + (lane & 7) + ((lane >> 3) & 1) * 8][8 * dt + (lane >> 4) * 8]);
-    mma16816(o[dt], pa, b[0], b[1]);
-    mma16816(o[dt + 1], pa, b[2], b[3]);
-  }
-}
-
-// exp rule of ops_simd.go:70-82 on a score x already reduced by the max.
-__device__ __forceinline__ float ref_exp(float x) { return x < -10.f ? 0.f : expf(x); }
-
-// Normalise and store 16 rows x 64 dims (rows q0 and q0+8 of this lane).
-__device__ __forceinline__ void store_rows(__half* out, long ldo, int L, int q0, float (*o)[4], float l0, float l1) {
-  const int tq = threadIdx.x & 3;
-  const float inv0 = 1.0f / l0, inv1 = 1.0f / l1;
-#pragma unroll
-  for (int dt = 0; dt < 8; dt++) {
-    const int d = dt * 8 + tq * 2;
-    if (q0 < L) *reinterpret_cast<uint32_t*>(out + (long)q0 * ldo + d) = pack_half2(o[dt][0] * inv0, o[dt][1] * inv0);
-    if (q0 + 8 < L)
-      *reinterpret_cast<uint32_t*>(out + (long)(q0 + 8) * ldo + d) = pack_half2(o[dt][2] * inv1, o[dt][3] * inv1);
-  }
-}
-
 }  // namespace
 
 __global__ void __launch_bounds__(SH_WARPS * 32) attention_short_kernel(const __half* __restrict__ qkv,
@@ -145,63 +81,10 @@ __global__ void __launch_bounds__(SH_WARPS * 32) attention_short_kernel(const __
   load_rows_async(sV, base + 2 * H, ld, 0, Lp, L);
   asm volatile("cp.async.wait_all;" ::: "memory");
   __syncthreads();
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, tq = lane & 3;
+  const int warp = threadIdx.x >> 5;
   const int qrow0 = qb * SH_QROWS + warp * 16;
   if (qrow0 >= L) return;
-  uint32_t qa[4][4];
-  load_q_frags(qa, sQ, warp * 16);
-
-  float sc[SH_MAXL / 8][4];
-#pragma unroll
-  for (int n = 0; n < SH_MAXL / 8; n++) {
-    sc[n][0] = sc[n][1] = sc[n][2] = sc[n][3] = 0.f;
-    if (n * 8 < Lp) qk_tile(sc[n], qa, sK, n * 8);
-  }
-  float mx0 = -INFINITY, mx1 = -INFINITY;
-#pragma unroll
-  for (int n = 0; n < SH_MAXL / 8; n++) {
-    const int key = n * 8 + tq * 2;
-#pragma unroll
-    for (int j = 0; j < 4; j++) {
-      const float v = (key + (j & 1) < L) ? sc[n][j] * 0.125f : -INFINITY;
-      sc[n][j] = v;
-      if (j < 2) mx0 = fmaxf(mx0, v);
-      else mx1 = fmaxf(mx1, v);
-    }
-  }
-#pragma unroll
-  for (int o = 1; o <= 2; o <<= 1) {
-    mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, o));
-    mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, o));
-  }
-  float l0 = 0.f, l1 = 0.f;
-#pragma unroll
-  for (int n = 0; n < SH_MAXL / 8; n++) {
-    sc[n][0] = ref_exp(__fsub_rn(sc[n][0], mx0));
-    sc[n][1] = ref_exp(__fsub_rn(sc[n][1], mx0));
-    sc[n][2] = ref_exp(__fsub_rn(sc[n][2], mx1));
-    sc[n][3] = ref_exp(__fsub_rn(sc[n][3], mx1));
-    l0 += sc[n][0] + sc[n][1];
-    l1 += sc[n][2] + sc[n][3];
-  }
-#pragma unroll
-  for (int o = 1; o <= 2; o <<= 1) {
-    l0 += __shfl_xor_sync(0xffffffffu, l0, o);
-    l1 += __shfl_xor_sync(0xffffffffu, l1, o);
-  }
-  float acc[8][4];
-#pragma unroll
-  for (int i = 0; i < 8; i++) acc[i][0] = acc[i][1] = acc[i][2] = acc[i][3] = 0.f;
-#pragma unroll
-  for (int c = 0; c < SH_MAXL / 16; c++) {
-    if (c * 16 < Lp) {
-      const uint32_t pa[4] = {pack_half2(sc[2 * c][0], sc[2 * c][1]), pack_half2(sc[2 * c][2], sc[2 * c][3]),
-                              pack_half2(sc[2 * c + 1][0], sc[2 * c + 1][1]),
-                              pack_half2(sc[2 * c + 1][2], sc[2 * c + 1][3])};
-      pv_chunk(acc, pa, sV, c * 16);
-    }
-  }
-  store_rows(out + (long)t0 * H + head * HD, H, L, qrow0 + g, acc, l0, l1);
+  attn_rows16<SH_MAXL>(sQ, warp * 16, sK, sV, L, out + (long)t0 * H + head * HD, H, qrow0);
 }
 
 __global__ void __launch_bounds__(128) attention_long_kernel(const __half* __restrict__ qkv,

@@ -8,6 +8,7 @@
 #include "common.cuh"
 #include "gguf_decode.cuh"
 #include "kernels.h"
+#include "ln_warp.cuh"
 
 namespace le {
 
@@ -74,29 +75,17 @@ __global__ void __launch_bounds__(256) ln_rows_kernel(const float* in, const flo
   float s = 0.f, ss = 0.f;
 #pragma unroll
   for (int i = 0; i < LN_MAXV; i++)
-    if (i < nv) {
-      s += x[i].x + x[i].y + x[i].z + x[i].w;
-      ss += x[i].x * x[i].x + x[i].y * x[i].y + x[i].z * x[i].z + x[i].w * x[i].w;
-    }
-  s = warp_sum(s);
-  ss = warp_sum(ss);
-  const float nf = (float)H;
-  const float mean = __fdiv_rn(s, nf);
-  const float var = __fsub_rn(__fdiv_rn(ss, nf), __fmul_rn(mean, mean));
-  const float inv = (float)(1.0 / sqrt((double)__fadd_rn(var, eps)));
+    if (i < nv) ln_accum(x[i], s, ss);
+  float mean, inv;
+  ln_finish(s, ss, H, eps, &mean, &inv);
   float* o32 = out32 + (long)warp * H;
   __half* o16 = out16 + (long)warp * H;
 #pragma unroll
   for (int i = 0; i < LN_MAXV; i++)
     if (i < nv) {
       const int c = (i * 32 + lane) * 4;
-      const float4 ww = *reinterpret_cast<const float4*>(w + c);
-      const float4 bb = *reinterpret_cast<const float4*>(b + c);
-      float4 y;
-      y.x = __fadd_rn(__fmul_rn(__fmul_rn(__fsub_rn(x[i].x, mean), inv), ww.x), bb.x);
-      y.y = __fadd_rn(__fmul_rn(__fmul_rn(__fsub_rn(x[i].y, mean), inv), ww.y), bb.y);
-      y.z = __fadd_rn(__fmul_rn(__fmul_rn(__fsub_rn(x[i].z, mean), inv), ww.z), bb.z);
-      y.w = __fadd_rn(__fmul_rn(__fmul_rn(__fsub_rn(x[i].w, mean), inv), ww.w), bb.w);
+      const float4 y = ln_apply(x[i], mean, inv, *reinterpret_cast<const float4*>(w + c),
+                                *reinterpret_cast<const float4*>(b + c));
       *reinterpret_cast<float4*>(o32 + c) = y;
       uint2 h;
       h.x = pack_half2(y.x, y.y);

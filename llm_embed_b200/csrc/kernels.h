@@ -39,6 +39,49 @@ cudaError_t launch_gemm_simt(int qf, const uint8_t* W, int n_virtual, int K, con
 cudaError_t launch_gemm_tc2(int qf, const uint8_t* W, int n_virtual, int K, const __half* A, long lda,
                             const EpiParams& ep, DevStatus* status, cudaStream_t s);
 
+// forward_small.cu: the whole forward for at most SMALL_MAX_TOKENS tokens in
+// one cooperative kernel (nomic-bert shape only).
+constexpr int SMALL_HIDDEN = 768;
+constexpr int SMALL_FFN = 3072;
+constexpr int SMALL_HEADS = 12;
+constexpr int SMALL_MAX_TOKENS = 16;
+constexpr int SMALL_MAX_LAYERS = 24;
+
+struct SmallGemm {
+  const uint8_t* w;  // tile-blocked quantised weight
+  int qf;            // its QFmt
+  int K;
+  int n_pairs;       // output row pairs (epilogue.cuh pair_rows)
+  int mode;          // EpiMode of the step
+};
+struct SmallLayer {
+  SmallGemm g[4];  // qkv, attn_output, merged up/gate, down
+  const float *attn_w, *attn_b, *out_w, *out_b;
+};
+struct SmallParams {
+  int T, nseq, n_layers;
+  const int32_t* ids;
+  const int32_t* offsets;
+  int emb_type;
+  const uint8_t* emb;
+  long emb_row_bytes;
+  int vocab;
+  const float *type0, *embd_w, *embd_b;
+  float eps;
+  const float *rope_cos, *rope_sin;
+  int32_t* pos;   // [T] positions (written)
+  __half* qkv;    // [T][3H]
+  __half* att;    // [T][H]
+  float* y;       // [T][H]
+  __half* ff;     // [T][F]
+  float* h_out;   // [T][H] final hidden states
+  unsigned* barrier;
+  DevStatus* status;
+  SmallLayer layers[SMALL_MAX_LAYERS];
+};
+bool small_forward_supported(const SmallParams& p, int hidden, int ffn, int heads, int sms);
+cudaError_t launch_forward_small(const SmallParams& p, cudaStream_t s);
+
 // gemm_f16.cu
 cudaError_t launch_gemm_f16(const __half* W16, int n_virtual, int K, const __half* A, long lda, const EpiParams& ep,
                             DevStatus* status, cudaStream_t s);

@@ -33,9 +33,9 @@ class TensorDesc(C.Structure):
                 ("data", C.c_void_p), ("n_bytes", C.c_int64)]
 
 
-NCLASS = 8
+NCLASS = 9
 CLASS_NAMES = ("gemm_qkv", "gemm_attn_out", "gemm_ffn_upgate", "gemm_ffn_down", "attention", "layernorm",
-               "embed_ln", "positions_pool")
+               "embed_ln", "positions_pool", "fused_small")
 
 
 class Stats(C.Structure):

@@ -199,6 +199,28 @@ def test_batch_equals_single_bitwise(model_path):
         e.Close()
 
 
+@pytest.mark.parametrize("wtype", [synth.GGML_Q8_0, synth.GGML_Q4_K, synth.GGML_Q5_K, synth.GGML_Q6_K])
+def test_small_fused_forward(model_path, wtype):
+    """Calls of <= 16 tokens run the whole encoder in one cooperative kernel:
+    it matches the oracle, and each sequence equals, bit for bit, the same
+    sequence inside a 40-token batch run by the separate kernels."""
+    path = model_path(small_spec(weight_type=wtype, embd_type=wtype))
+    e = Embedder.Load(path)
+    try:
+        ids, offs = synth.make_ids([3, 7, 1, 5, 6, 9, 4, 5], seed=9, vocab=2048)
+        lens = np.diff(offs)
+        batch = e.EmbedIDs(ids, offs)                      # 40 tokens: separate kernels
+        first = e.EmbedIDs(ids[:16], offs[:5])             # 16 tokens: fused kernel
+        assert np.array_equal(first.view(np.uint32), batch[:4].view(np.uint32))
+        for i in range(len(lens)):
+            one = e.EmbedIDs(ids[offs[i]:offs[i + 1]], np.array([0, lens[i]], np.int32))
+            assert np.array_equal(one[0].view(np.uint32), batch[i].view(np.uint32)), f"sequence {i}"
+        ref = _oracle_embed(path, ids[:16], offs[:5])
+        assert_parity(first, ref)
+    finally:
+        e.Close()
+
+
 def test_graph_replay_matches_direct(model_path):
     """Small calls replay a captured CUDA graph after their first (direct)
     run: repeated calls, and device calls with other output pointers, give
