@@ -2,18 +2,22 @@
 API (internal/embed/embedder.go): Load, Embed, EmbedBatch, Dim,
 SetTargetDim, plus EmbedIDs for packed batches.
 
-Text tokenisation stays with the caller (the reference's WordPiece tokenizer,
-internal/embed/tokenizer.go, is host code outside this library): every call
-takes token ids.  There is no CPU fallback: if the CUDA library is missing or
-no sm_100 GPU is present, the calls raise.
+Texts are tokenised on the host (tokenizer.py, a restatement of
+internal/embed/tokenizer.go) with the model's GGUF vocabulary and the
+TaskPrefix, as Embedder.Embed does; the device library takes token ids, which
+Embed / EmbedBatch also accept directly.  There is no CPU fallback: if the
+CUDA library is missing or no sm_100 GPU is present, the calls raise.
 """
 from __future__ import annotations
 
 import ctypes as C
 import os
+import struct
 import threading
 
 import numpy as np
+
+from .tokenizer import WordPieceTokenizer
 
 _HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(_HERE, "libllmembed_cuda.so")
@@ -116,13 +120,16 @@ def pack(seqs) -> tuple[np.ndarray, np.ndarray]:
 class Embedder:
     """One model replica per device; EmbedIDs shards sequences across them."""
 
-    def __init__(self, handles, hp: HParams):
+    def __init__(self, handles, hp: HParams, tokenizer: WordPieceTokenizer | None = None):
         self._handles = (C.c_void_p * len(handles))(*handles)
         self._n = len(handles)
         self.hparams = hp
         self.target_dim = hp.hidden
+        self.tokenizer = tokenizer
+        # embedder.go:15, 39: prepended to every text before tokenisation.
+        self.TaskPrefix = "search_query: "
 
-    # embedder.go:19 Load
+    # embedder.go:19 Load: model replicas plus the GGUF's tokenizer.
     @classmethod
     def Load(cls, model_path: str, devices=(0,)) -> "Embedder":
         handles = []
@@ -137,7 +144,17 @@ class Embedder:
             raise
         hp = HParams()
         _check(lib().le_model_hparams(handles[0], C.byref(hp)))
-        return cls(handles, hp)
+        # The model file parsed, so its KV section is readable; a file without
+        # tokenizer.ggml.tokens still embeds token ids.
+        try:
+            tok = WordPieceTokenizer.Load(model_path)
+        except KeyError:
+            tok = None
+        except (OSError, ValueError, struct.error) as err:
+            for h in handles:
+                lib().le_model_free(h)
+            raise LlmEmbedError(LE_EIO, f"tokenizer: {err}") from err
+        return cls(handles, hp, tok)
 
     @classmethod
     def LoadTensors(cls, tensors, hp: HParams, devices=(0,)) -> "Embedder":
@@ -194,16 +211,27 @@ class Embedder:
                                   _p(out, C.c_float)))
         return out
 
-    # embedder.go:46 Embed (token ids in place of text)
-    def Embed(self, ids) -> np.ndarray:
-        i, o = pack([ids])
+    def Tokenize(self, text: str) -> list[int]:
+        """TaskPrefix + text through the model's tokenizer, truncated to the
+        context length (embedder.go:48-51)."""
+        if self.tokenizer is None:
+            raise LlmEmbedError(LE_EINVAL, "no tokenizer: load the model from a GGUF file with tokenizer.ggml.tokens")
+        return self.tokenizer.Encode(self.TaskPrefix + text, self.hparams.context_length)[0]
+
+    def _ids(self, item) -> list[int]:
+        return self.Tokenize(item) if isinstance(item, str) else item
+
+    # embedder.go:46 Embed: a text (or an already tokenised id sequence).
+    def Embed(self, text) -> np.ndarray:
+        i, o = pack([self._ids(text)])
         return self.EmbedIDs(i, o)[0]
 
-    # embedder.go:75 EmbedBatch: one device call for the whole batch.
-    def EmbedBatch(self, seqs) -> list[np.ndarray]:
-        if len(seqs) == 0:
+    # embedder.go:75 EmbedBatch: texts (or id sequences), one device call for
+    # the whole batch instead of one forward per text.
+    def EmbedBatch(self, texts) -> list[np.ndarray]:
+        if len(texts) == 0:
             return []
-        i, o = pack(seqs)
+        i, o = pack([self._ids(t) for t in texts])
         return list(self.EmbedIDs(i, o))
 
     def embed_device(self, d_ids: int, d_offsets: int, nseq: int, n_tokens: int, max_len: int, d_out: int,

@@ -243,8 +243,8 @@ def write_model(path: str, spec: ModelSpec) -> str:
     kv.append(_gguf_str("nomic-bert.attention.layer_norm_epsilon") + struct.pack("<If", 6, spec.eps))
     kv.append(_gguf_str("nomic-bert.rope.freq_base") + struct.pack("<If", 6, spec.rope_base))
     if spec.tokens:
-        special = {0: "[PAD]", 100: "[UNK]", 101: "[CLS]", 102: "[SEP]", 103: "[MASK]"}
-        toks = b"".join(_gguf_str(special.get(i, f"▁t{i}")) for i in range(spec.vocab))
+        vocab = synthetic_vocab(spec.vocab)
+        toks = b"".join(_gguf_str(t) for t in vocab)
         kv.append(_gguf_str("tokenizer.ggml.tokens") + struct.pack("<IIQ", 9, 8, spec.vocab) + toks)
     infos, blobs, off = [], [], 0
     for idx, (name, dims, gtype) in enumerate(tensors):
@@ -265,6 +265,33 @@ def write_model(path: str, spec: ModelSpec) -> str:
     return path
 
 
+# Synthetic vocabulary: the specials at their BERT ids, then (from id 1000)
+# whole words with the SentencePiece prefix, sub-word pieces, letters, digits
+# and punctuation with and without the prefix, two CJK characters; the rest
+# are filler "▁t<id>" entries.  Enough for the tokenizer's greedy
+# matching, fallbacks and [UNK] paths to all occur on ordinary text.
+VOCAB_VERSION = 2
+_VOCAB_WORDS = ("hello world search query document what is machine learning the cat sat on mat how to cook "
+                "pasta quantum computing basics go programming language neural network architecture climate "
+                "change effects embedding model a of and in for un token caf \u00fcber").split()
+_VOCAB_PIECES = ("ing", "ed", "s", "er", "ly", "ation", "iz", "izer", "able", "ld", "wor", "ize", "ization")
+_VOCAB_CHARS = "abcdefghijklmnopqrstuvwxyz0123456789"
+_VOCAB_PUNCT = ".,!?;:'\"()-_/"
+
+
+def synthetic_vocab(n: int) -> list[str]:
+    special = {0: "[PAD]", 100: "[UNK]", 101: "[CLS]", 102: "[SEP]", 103: "[MASK]"}
+    entries = ["\u2581" + w for w in _VOCAB_WORDS] + list(_VOCAB_PIECES)
+    entries += ["\u2581" + c for c in _VOCAB_CHARS] + list(_VOCAB_CHARS)
+    entries += ["\u2581" + c for c in _VOCAB_PUNCT] + ["\u2581\u4e2d", "\u2581\u6587"]
+    entries = list(dict.fromkeys(entries))  # unique, first occurrence kept
+    vocab = [special.get(i, f"\u2581t{i}") for i in range(n)]
+    for j, e in enumerate(entries):
+        if 1000 + j < n:
+            vocab[1000 + j] = e
+    return vocab
+
+
 def cached_model(name_or_spec, directory: str | None = None) -> str:
     """Path of a synthetic model, written once into `directory` (default
     $LLMEMBED_MODEL_DIR or /tmp/llm_embed_b200_models)."""
@@ -272,7 +299,8 @@ def cached_model(name_or_spec, directory: str | None = None) -> str:
     directory = directory or os.environ.get("LLMEMBED_MODEL_DIR", "/tmp/llm_embed_b200_models")
     os.makedirs(directory, exist_ok=True)
     tag = "_".join(str(x) for x in (spec.layers, spec.hidden, spec.heads, spec.ffn, spec.vocab, spec.context,
-                                      spec.embd_type, *spec.weight_types, spec.seed, int(spec.tokens)))
+                                      spec.embd_type, *spec.weight_types, spec.seed,
+                                      int(spec.tokens) * VOCAB_VERSION))
     path = os.path.join(directory, f"nomic_{tag}.gguf")
     if not os.path.exists(path):
         write_model(path, spec)

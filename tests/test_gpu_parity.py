@@ -221,6 +221,53 @@ def test_small_fused_forward(model_path, wtype):
         e.Close()
 
 
+REF_TEXTS = ["hello world", "what is machine learning", "the cat sat on the mat", "how to cook pasta",
+             "quantum computing basics", "go programming language", "neural network architecture",
+             "climate change effects"]
+
+
+def test_embed_text_api(model_path):
+    """Embed(text) = TaskPrefix + text through the GGUF's tokenizer, then the
+    forward (embedder.go:46-70): equal to embedding those ids, and to the
+    oracle; Matryoshka truncation through the text API (TestSetTargetDim)."""
+    path = model_path(small_spec())
+    e = Embedder.Load(path)
+    try:
+        assert e.TaskPrefix == "search_query: "
+        ids = e.tokenizer.Encode("search_query: hello world", e.hparams.context_length)[0]
+        v = e.Embed("hello world")
+        assert np.array_equal(v.view(np.uint32), e.Embed(ids).view(np.uint32))
+        ref = _oracle_embed(path, np.asarray(ids, np.int32), np.array([0, len(ids)], np.int32))
+        assert_parity(v[None], ref)
+        assert abs(np.linalg.norm(v) - 1.0) < 1e-5
+        e.TaskPrefix = ""
+        assert not np.array_equal(e.Embed("hello world"), v)
+        e.TaskPrefix = "search_query: "
+        e.SetTargetDim(256)
+        t = e.Embed("hello world")
+        assert t.shape == (256,) and abs(np.linalg.norm(t) - 1.0) < 1e-5
+    finally:
+        e.Close()
+
+
+def test_embed_batch_texts_match_singles(model_path):
+    """TestEmbedBatchParallel (embedder_test.go:212-253) on its eight texts.
+    The reference runs one forward per text, so its batch equals its singles
+    bit for bit.  Here the batch (76 tokens) runs the tensor-core GEMMs and
+    each single (<= 16 tokens) the single-kernel path: equal within the
+    parity tolerance, and bit for bit when the batch stays below 64 tokens."""
+    e = Embedder.Load(model_path(small_spec()))
+    try:
+        batch = e.EmbedBatch(REF_TEXTS)
+        singles = [e.Embed(t) for t in REF_TEXTS]
+        assert_parity(np.stack(batch), np.stack(singles))
+        small = e.EmbedBatch(REF_TEXTS[:4])  # 40 tokens
+        for t, b in zip(REF_TEXTS[:4], small):
+            assert np.array_equal(e.Embed(t).view(np.uint32), b.view(np.uint32))
+    finally:
+        e.Close()
+
+
 def test_graph_replay_matches_direct(model_path):
     """Small calls replay a captured CUDA graph after their first (direct)
     run: repeated calls, and device calls with other output pointers, give
