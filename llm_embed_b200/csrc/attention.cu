@@ -63,7 +63,7 @@ __device__ __forceinline__ void load_rows_async(__half (*dst)[LDS], const __half
 
 }  // namespace
 
-__global__ void __launch_bounds__(SH_WARPS * 32) attention_short_kernel(const __half* __restrict__ qkv,
+__global__ void __launch_bounds__(SH_WARPS * 32, 4) attention_short_kernel(const __half* __restrict__ qkv,
                                                                        const int32_t* __restrict__ offsets, int H,
                                                                        __half* __restrict__ out) {
   const int qb = blockIdx.x, head = blockIdx.y, s = blockIdx.z;

@@ -103,16 +103,20 @@ __device__ __forceinline__ void attn_rows16(__half (*sQ)[LDS], int qrow_local, _
     sc[n][0] = sc[n][1] = sc[n][2] = sc[n][3] = 0.f;
     if (n * 8 < Lp) qk_tile(sc[n], qa, sK, n * 8);
   }
+  // Tiles at or past Lp hold only masked keys: their weights are exactly 0,
+  // so skipping them leaves the maxima, the sums and O unchanged.
   float mx0 = -INFINITY, mx1 = -INFINITY;
 #pragma unroll
   for (int n = 0; n < MAXL / 8; n++) {
-    const int key = n * 8 + tq * 2;
+    if (n * 8 < Lp) {
+      const int key = n * 8 + tq * 2;
 #pragma unroll
-    for (int j = 0; j < 4; j++) {
-      const float v = (key + (j & 1) < L) ? sc[n][j] * 0.125f : -INFINITY;
-      sc[n][j] = v;
-      if (j < 2) mx0 = fmaxf(mx0, v);
-      else mx1 = fmaxf(mx1, v);
+      for (int j = 0; j < 4; j++) {
+        const float v = (key + (j & 1) < L) ? sc[n][j] * 0.125f : -INFINITY;
+        sc[n][j] = v;
+        if (j < 2) mx0 = fmaxf(mx0, v);
+        else mx1 = fmaxf(mx1, v);
+      }
     }
   }
 #pragma unroll
@@ -123,12 +127,14 @@ __device__ __forceinline__ void attn_rows16(__half (*sQ)[LDS], int qrow_local, _
   float l0 = 0.f, l1 = 0.f;
 #pragma unroll
   for (int n = 0; n < MAXL / 8; n++) {
-    sc[n][0] = ref_exp(__fsub_rn(sc[n][0], mx0));
-    sc[n][1] = ref_exp(__fsub_rn(sc[n][1], mx0));
-    sc[n][2] = ref_exp(__fsub_rn(sc[n][2], mx1));
-    sc[n][3] = ref_exp(__fsub_rn(sc[n][3], mx1));
-    l0 += sc[n][0] + sc[n][1];
-    l1 += sc[n][2] + sc[n][3];
+    if (n * 8 < Lp) {
+      sc[n][0] = ref_exp(__fsub_rn(sc[n][0], mx0));
+      sc[n][1] = ref_exp(__fsub_rn(sc[n][1], mx0));
+      sc[n][2] = ref_exp(__fsub_rn(sc[n][2], mx1));
+      sc[n][3] = ref_exp(__fsub_rn(sc[n][3], mx1));
+      l0 += sc[n][0] + sc[n][1];
+      l1 += sc[n][2] + sc[n][3];
+    }
   }
 #pragma unroll
   for (int o = 1; o <= 2; o <<= 1) {
