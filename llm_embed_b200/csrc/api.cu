@@ -419,6 +419,9 @@ static int forward(le_model* m, const int32_t* d_ids, const int32_t* d_offsets, 
       e.rope_cols = 2 * H;
       TRY(gemm(m, 0, L.qkv, hA, H, e, s));
       PLAUNCH(4, launch_attention(qkv, d_offsets, nseq, max_len, H, m->hp.heads, m->head_dim, att, s));
+      if (max_len > ATTN_SHORT_MAX)
+        PLAUNCH(4, launch_attention_tc(qkv, d_offsets, nseq, T, max_len, ATTN_SHORT_MAX + 1, H, m->hp.heads, att,
+                                       m->status.as<DevStatus>(), s));
       EpiParams r{};
       r.M = T;
       r.mode = EPI_F32;

@@ -27,9 +27,13 @@ cudaError_t launch_pool(const float* h, const int32_t* offsets, int nseq, int H,
 cudaError_t launch_f32_to_f16(const float* in, long n, __half* out, cudaStream_t s);
 cudaError_t launch_positions(const int32_t* offsets, int nseq, int32_t* pos, cudaStream_t s);
 
-// attention.cu
+// attention.cu: sequences of at most ATTN_SHORT_MAX tokens (mma.sync tiles)
+constexpr int ATTN_SHORT_MAX = 128;
 cudaError_t launch_attention(const __half* qkv, const int32_t* offsets, int nseq, int max_len, int H, int heads,
                              int head_dim, __half* out, cudaStream_t s);
+// attention_tc.cu: sequences of at least min_len tokens (tcgen05), T = rows of qkv
+cudaError_t launch_attention_tc(const __half* qkv, const int32_t* offsets, int nseq, int T, int max_len, int min_len,
+                                int H, int heads, __half* out, DevStatus* status, cudaStream_t s);
 
 // gemm_simt.cu
 cudaError_t launch_gemm_simt(int qf, const uint8_t* W, int n_virtual, int K, const __half* A, long lda,
