@@ -30,6 +30,7 @@ namespace {
 using namespace attn;
 
 constexpr int SH_MAXL = 128;
+static_assert(ATTN_SHORT_MAX <= SH_MAXL, "short-kernel length class");
 constexpr int SH_QROWS = 64;
 constexpr int SH_WARPS = SH_QROWS / 16;
 constexpr int SH_SMEM = (SH_QROWS + 2 * SH_MAXL) * LDS * 2;
@@ -56,7 +57,7 @@ __global__ void __launch_bounds__(SH_WARPS * 32, 4) attention_short_kernel(const
   const int qb = blockIdx.x, head = blockIdx.y, s = blockIdx.z;
   const int t0 = offsets[s];
   const int L = offsets[s + 1] - t0;
-  if (L == 0 || L > SH_MAXL || qb * SH_QROWS >= L) return;
+  if (L == 0 || L > ATTN_SHORT_MAX || qb * SH_QROWS >= L) return;
   extern __shared__ __align__(16) uint8_t smem_attn[];
   __half(*sQ)[LDS] = reinterpret_cast<__half(*)[LDS]>(smem_attn);
   __half(*sK)[LDS] = sQ + SH_QROWS;
