@@ -58,6 +58,55 @@ __device__ __forceinline__ float geglu(float v, float u) {
   return fmaf(hv, th, hv);
 }
 
+// Two-lane fp32 arithmetic (sm_100 packed f32x2: one instruction, two IEEE
+// round-to-nearest results, the same as the scalar operations).
+__device__ __forceinline__ unsigned long long f2_pack(float a, float b) {
+  unsigned long long r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(a), "f"(b));
+  return r;
+}
+__device__ __forceinline__ void f2_unpack(unsigned long long r, float& a, float& b) {
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(a), "=f"(b) : "l"(r));
+}
+__device__ __forceinline__ unsigned long long f2_mul(unsigned long long a, unsigned long long b) {
+  unsigned long long r;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
+__device__ __forceinline__ unsigned long long f2_add(unsigned long long a, unsigned long long b) {
+  unsigned long long r;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
+__device__ __forceinline__ unsigned long long f2_fma(unsigned long long a, unsigned long long b, unsigned long long c) {
+  unsigned long long r;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(a), "l"(b), "l"(c));
+  return r;
+}
+
+// geglu() of two (gate, up) pairs, as fp16x2: the same operations in the
+// same order, two lanes per instruction (the reciprocal stays per element).
+__device__ __forceinline__ uint32_t geglu2(float v0, float v1, float u0, float u1) {
+  const unsigned long long v = f2_pack(v0, v1);
+  const unsigned long long t = f2_mul(v, f2_fma(f2_pack(0.0356774081f, 0.0356774081f), f2_mul(v, v),
+                                                f2_pack(0.7978845608f, 0.7978845608f)));
+  const unsigned long long t2 = f2_mul(t, t);
+  const unsigned long long num = f2_add(f2_pack(27.0f, 27.0f), t2);
+  const unsigned long long den = f2_fma(f2_pack(9.0f, 9.0f), t2, f2_pack(27.0f, 27.0f));
+  float n0, n1, d0, d1, t0, t1;
+  f2_unpack(num, n0, n1);
+  f2_unpack(den, d0, d1);
+  f2_unpack(t, t0, t1);
+  float th0, th1;
+  f2_unpack(f2_mul(t, f2_pack(__fdividef(n0, d0), __fdividef(n1, d1))), th0, th1);
+  th0 = fabsf(t0) > 4.97f ? copysignf(1.0f, t0) : th0;
+  th1 = fabsf(t1) > 4.97f ? copysignf(1.0f, t1) : th1;
+  const unsigned long long hv = f2_mul(f2_mul(f2_pack(0.5f, 0.5f), v), f2_pack(u0, u1));
+  float o0, o1;
+  f2_unpack(f2_fma(hv, f2_pack(th0, th1), hv), o0, o1);
+  return pack_half2(o0, o1);
+}
+
 // Epilogue of one 256-column pair tile for the calling warp: accumulator
 // columns [c_begin, c_end) of TMEM address `tbase` (its lane quarter already
 // added), output rows row0 .. row0+31, tile column origin n0 (virtual rows of
@@ -102,7 +151,7 @@ __device__ __forceinline__ void epilogue_tile(const EpiParams& ep, const CUtenso
         tmem_ld16(tbase + c + 16 * h + GEGLU_HALF, gt);
 #pragma unroll
         for (int i = 0; i < 8; i++)
-          words[8 * h + i] = pack_half2(geglu(gt[2 * i], up[2 * i]), geglu(gt[2 * i + 1], up[2 * i + 1]));
+          words[8 * h + i] = geglu2(gt[2 * i], gt[2 * i + 1], up[2 * i], up[2 * i + 1]);
       }
       emit_block(tmap_out, stage, buf, words, (n0 + c) / TILE_N * GEGLU_HALF, row0);
     }
