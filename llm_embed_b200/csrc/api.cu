@@ -135,6 +135,7 @@ struct Layer {
 struct Workspace {
   int cap_tokens = 0, cap_seqs = 0;
   DevBuf ids, offsets, pos, h32, y32, hA, qkv, att, ff, out;
+  DevBuf ln_part, ln_ctl;  // row statistics of the fused projection + LayerNorm
   HostBuf h_ids, h_offsets, h_out;
 };
 
@@ -313,6 +314,11 @@ static int ensure_ws(le_model* m, int tokens, int seqs) {
     TRY(w.att.ensure(T * H * 2));
     TRY(w.ff.ensure(T * F * 2));
     TRY(w.h_ids.ensure(T * 4));
+    TRY(w.ln_part.ensure(gemm_ln_part_bytes((int)T)));
+    TRY(w.ln_ctl.ensure(16));
+    CK(cudaMemsetAsync(w.ln_part.p, 0xFF, gemm_ln_part_bytes((int)T), m->stream));
+    CK(cudaMemsetAsync(w.ln_ctl.p, 0, 16, m->stream));
+    CK(cudaStreamSynchronize(m->stream));  // before forward() on any stream
     w.cap_tokens = (int)T;
   }
   if (seqs > w.cap_seqs) {
@@ -324,6 +330,18 @@ static int ensure_ws(le_model* m, int tokens, int seqs) {
     w.cap_seqs = (int)S;
   }
   return LE_OK;
+}
+
+// check_status of a model; after a device error the fused LayerNorm's
+// statistics words may be left filled, so they return to the empty marker.
+static int model_status(le_model* m, cudaStream_t s) {
+  const int rc = check_status(m->status, s);
+  if (rc != LE_OK && m->ws.cap_tokens > 0) {
+    cudaMemsetAsync(m->ws.ln_part.p, 0xFF, gemm_ln_part_bytes(m->ws.cap_tokens), s);
+    cudaMemsetAsync(m->ws.ln_ctl.p, 0, 16, s);
+    cudaStreamSynchronize(s);
+  }
+  return rc;
 }
 
 // ---------------------------------------------------------- forward -------
@@ -357,6 +375,9 @@ static int forward(le_model* m, const int32_t* d_ids, const int32_t* d_offsets, 
   __half* att = w.att.as<__half>();
   __half* ff = w.ff.as<__half>();
   int32_t* pos = w.pos.as<int32_t>();
+  unsigned long long* ln_part = w.ln_part.as<unsigned long long>();
+  unsigned* ln_ctl = w.ln_ctl.as<unsigned>();
+  const int ln_rows = gemm_ln_part_rows(w.cap_tokens);
   if (T > 0 && T <= SMALL_MAX_TOKENS && (int)m->layers.size() <= SMALL_MAX_LAYERS) {
     // A few tokens: the whole encoder in one cooperative kernel, then the pool.
     SmallParams sp{};
@@ -405,6 +426,9 @@ static int forward(le_model* m, const int32_t* d_ids, const int32_t* d_offsets, 
     PLAUNCH(6, launch_embed_ln(d_ids, m->emb_type, m->emb.as<uint8_t>(), m->emb_row_bytes, m->vocab,
                                m->type0.as<float>(), m->embd_w.as<float>(), m->embd_b.as<float>(), m->hp.ln_eps, T,
                                H, h32, hA, m->status.as<DevStatus>(), s));
+    // Large batches: the out and down projections carry the residual add
+    // and LayerNorm in their epilogue (same bits as GEMM + launch_ln_add).
+    const bool fuse_ln = T >= TC_F16_MIN_M && gemm_ln_supported(H, H) && gemm_ln_supported(H, F);
     for (const Layer& L : m->layers) {
       EpiParams e{};
       e.M = T;
@@ -428,8 +452,14 @@ static int forward(le_model* m, const int32_t* d_ids, const int32_t* d_offsets, 
       r.N = H;
       r.out32 = y32;
       r.ldo = H;
-      TRY(gemm(m, 1, L.out, att, H, r, s));
-      PLAUNCH(5, launch_ln_add(h32, y32, L.attn_w.as<float>(), L.attn_b.as<float>(), m->hp.ln_eps, T, H, h32, hA, s));
+      if (fuse_ln) {
+        PLAUNCH(1, launch_gemm_ln(L.out.w16.as<__half>(), H, att, H, T, h32, hA, L.attn_w.as<float>(),
+                                  L.attn_b.as<float>(), m->hp.ln_eps, ln_part, ln_rows, ln_ctl, m->status.as<DevStatus>(), s));
+      } else {
+        TRY(gemm(m, 1, L.out, att, H, r, s));
+        PLAUNCH(5,
+                launch_ln_add(h32, y32, L.attn_w.as<float>(), L.attn_b.as<float>(), m->hp.ln_eps, T, H, h32, hA, s));
+      }
       EpiParams g{};
       g.M = T;
       g.mode = EPI_GEGLU;
@@ -437,8 +467,13 @@ static int forward(le_model* m, const int32_t* d_ids, const int32_t* d_offsets, 
       g.out16 = ff;
       g.ldo = F;
       TRY(gemm(m, 2, L.upgate, hA, H, g, s));
-      TRY(gemm(m, 3, L.down, ff, F, r, s));
-      PLAUNCH(5, launch_ln_add(h32, y32, L.out_w.as<float>(), L.out_b.as<float>(), m->hp.ln_eps, T, H, h32, hA, s));
+      if (fuse_ln) {
+        PLAUNCH(3, launch_gemm_ln(L.down.w16.as<__half>(), F, ff, F, T, h32, hA, L.out_w.as<float>(),
+                                  L.out_b.as<float>(), m->hp.ln_eps, ln_part, ln_rows, ln_ctl, m->status.as<DevStatus>(), s));
+      } else {
+        TRY(gemm(m, 3, L.down, ff, F, r, s));
+        PLAUNCH(5, launch_ln_add(h32, y32, L.out_w.as<float>(), L.out_b.as<float>(), m->hp.ln_eps, T, H, h32, hA, s));
+      }
     }
   }
   PLAUNCH(7, launch_pool(h32, d_offsets, nseq, H, out_dim, d_out, s));
@@ -517,7 +552,7 @@ static int embed_host(le_model* m, const int32_t* ids, const int32_t* offs, int 
     CK(cudaMemcpyAsync(w.offsets.p, ho, (size_t)(n + 1) * 4, cudaMemcpyHostToDevice, s));
     TRY(run_forward(m, w.ids.as<int32_t>(), w.offsets.as<int32_t>(), n, T, maxlen, out_dim, w.out.as<float>(), s));
     CK(cudaMemcpyAsync(w.h_out.p, w.out.p, (size_t)n * out_dim * 4, cudaMemcpyDeviceToHost, s));
-    TRY(check_status(m->status, s));
+    TRY(model_status(m, s));
     std::memcpy(out + (size_t)s0 * out_dim, w.h_out.p, (size_t)n * out_dim * 4);
     s0 = s1;
   }
@@ -907,7 +942,7 @@ int le_sync(le_model* m) {
   std::lock_guard<std::mutex> lk(m->mu);
   CK(cudaSetDevice(m->dev));
   CK(cudaDeviceSynchronize());
-  return check_status(m->status, m->stream);
+  return model_status(m, m->stream);
 }
 
 int le_set_profiling(le_model* m, int enable) {

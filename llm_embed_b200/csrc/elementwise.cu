@@ -72,12 +72,8 @@ __global__ void __launch_bounds__(256) ln_rows_kernel(const float* in, const flo
         x[i] = make_float4(__fadd_rn(a.x, b.x), __fadd_rn(a.y, b.y), __fadd_rn(a.z, b.z), __fadd_rn(a.w, b.w));
       }
   }
-  float s = 0.f, ss = 0.f;
-#pragma unroll
-  for (int i = 0; i < LN_MAXV; i++)
-    if (i < nv) ln_accum(x[i], s, ss);
   float mean, inv;
-  ln_finish(s, ss, H, eps, &mean, &inv);
+  ln_row_stats(x, nv, H, eps, &mean, &inv);
   float* o32 = out32 + (long)warp * H;
   __half* o16 = out16 + (long)warp * H;
 #pragma unroll

@@ -173,7 +173,6 @@ __device__ void ln_rows(float* h, __half* x, const float* y, const float* w, con
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   for (int t = warp; t < T; t += NWARPS) {
     float4 v[H / 128];
-    float s = 0.f, ss = 0.f;
 #pragma unroll
     for (int i = 0; i < H / 128; i++) {
       const int c = (i * 32 + lane) * 4;
@@ -183,10 +182,9 @@ __device__ void ln_rows(float* h, __half* x, const float* y, const float* w, con
         a = make_float4(__fadd_rn(a.x, d.x), __fadd_rn(a.y, d.y), __fadd_rn(a.z, d.z), __fadd_rn(a.w, d.w));
       }
       v[i] = a;
-      ln_accum(a, s, ss);
     }
     float mean, inv;
-    ln_finish(s, ss, H, eps, &mean, &inv);
+    ln_row_stats(v, H / 128, H, eps, &mean, &inv);
 #pragma unroll
     for (int i = 0; i < H / 128; i++) {
       const int c = (i * 32 + lane) * 4;

@@ -86,6 +86,19 @@ struct SmallParams {
 bool small_forward_supported(const SmallParams& p, int hidden, int ffn, int heads, int sms);
 cudaError_t launch_forward_small(const SmallParams& p, cudaStream_t s);
 
+// gemm_ln.cu: projection to 768 columns with the residual add and
+// LayerNorm fused: h = LN(h + A . W16^T), h in place, out16 = fp16(h).
+// part (gemm_ln_part_bytes, sized for part_rows = gemm_ln_part_rows(M) or
+// more) holds the rows' chunk statistics and ctl two counters (16 bytes);
+// before the first launch and after any device error part must be all
+// 0xFF bytes and ctl zero.
+bool gemm_ln_supported(int N, int K);
+int gemm_ln_part_rows(int M);
+size_t gemm_ln_part_bytes(int M);
+cudaError_t launch_gemm_ln(const __half* W16, int K, const __half* A, long lda, int M, float* h, __half* out16,
+                           const float* ln_w, const float* ln_b, float eps, unsigned long long* part, int part_rows,
+                           unsigned* ctl, DevStatus* status, cudaStream_t s);
+
 // gemm_f16.cu
 cudaError_t launch_gemm_f16(const __half* W16, int n_virtual, int K, const __half* A, long lda, const EpiParams& ep,
                             DevStatus* status, cudaStream_t s);

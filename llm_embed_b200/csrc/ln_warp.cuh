@@ -1,7 +1,8 @@
-// One warp's LayerNorm of a row (ops_simd.go:7-24), shared by the row
-// kernels (elementwise.cu) and the single-kernel small forward
-// (forward_small.cu) so both give the same bits: every add and multiply is
-// explicitly rounded (no contraction), sums reduce in a fixed butterfly.
+// LayerNorm of a row (ops_simd.go:7-24), shared by the row kernels
+// (elementwise.cu), the single-kernel small forward (forward_small.cu) and
+// the fused projection + LayerNorm kernel (gemm_ln.cu) so all give the same
+// bits: every add and multiply is explicitly rounded (no contraction), sums
+// reduce in one fixed order (ln_row_stats).
 #pragma once
 #include "common.cuh"
 
@@ -14,18 +15,41 @@ __device__ __forceinline__ void ln_accum(const float4 a, float& s, float& ss) {
                                __fmul_rn(a.w, a.w)));
 }
 
-// Warp totals -> mean and float32(1 / sqrt(float64(var + eps))), with
+// float32(1 / sqrt(float64(var + eps))) of the row totals, with
 // var = sumSq / n - mean^2 (single pass, float32).
-__device__ __forceinline__ void ln_finish(float s, float ss, int n, float eps, float* mean, float* inv) {
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) {
-    s = __fadd_rn(s, __shfl_xor_sync(0xffffffffu, s, o));
-    ss = __fadd_rn(ss, __shfl_xor_sync(0xffffffffu, ss, o));
-  }
+__device__ __forceinline__ void ln_stats(float s, float ss, int n, float eps, float* mean, float* inv) {
   const float nf = (float)n;
   *mean = __fdiv_rn(s, nf);
   const float var = __fsub_rn(__fdiv_rn(ss, nf), __fmul_rn(*mean, *mean));
   *inv = (float)(1.0 / sqrt((double)__fadd_rn(var, eps)));
+}
+
+// Row statistics of one warp's row.  Lane l holds float4 chunk i at columns
+// (32 i + l) * 4, i < nv.  Each 128-column chunk reduces on its own: the
+// lane's four values (ln_accum from zero), then a fixed butterfly over the
+// lanes (xor 16, 8, 4, 2, 1); the chunk totals add in column order.  The
+// fused projection + LayerNorm kernel (gemm_ln.cu), whose warps each own one
+// chunk of a row, repeats exactly these operations, so every path gives the
+// same bits.
+template <int MAXV>
+__device__ __forceinline__ void ln_row_stats(const float4 (&x)[MAXV], int nv, int n, float eps, float* mean,
+                                             float* inv) {
+  float ts = 0.f, tss = 0.f;
+#pragma unroll
+  for (int i = 0; i < MAXV; i++) {
+    if (i < nv) {
+      float s = 0.f, ss = 0.f;
+      ln_accum(x[i], s, ss);
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) {
+        s = __fadd_rn(s, __shfl_xor_sync(0xffffffffu, s, o));
+        ss = __fadd_rn(ss, __shfl_xor_sync(0xffffffffu, ss, o));
+      }
+      ts = __fadd_rn(ts, s);
+      tss = __fadd_rn(tss, ss);
+    }
+  }
+  ln_stats(ts, tss, n, eps, mean, inv);
 }
 
 // (x - mean) * inv * w + b.

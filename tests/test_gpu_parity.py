@@ -450,6 +450,29 @@ def test_gemm_paths_bitwise_equal(qtype):
         qw.close()
 
 
+def test_large_batch_rows_match_mid_batch(model_path):
+    """Batches of 256+ tokens run the out/down projections with the residual
+    LayerNorm fused into the GEMM (three CTA pairs per 256-row block, row
+    statistics exchanged through global memory); 64..255 tokens run GEMM +
+    separate LayerNorm.  Both reduce each row in the same order, so a
+    sequence's embedding is the same bits in either, including in a batch
+    whose last token tile is partial."""
+    spec = small_spec()
+    e = Embedder.Load(model_path(spec))
+    try:
+        lens = [37, 5, 61, 18, 29, 44, 90, 12, 73, 55, 8, 101, 66, 23, 48, 77, 31, 59]  # 939 tokens
+        ids, offs = synth.make_ids(lens, seed=11, vocab=spec.vocab)
+        big = e.EmbedIDs(ids, offs)
+        k = 4  # 121 tokens
+        mid = e.EmbedIDs(ids[:offs[k]], offs[:k + 1])
+        assert offs[k] >= 64 and offs[-1] >= 256 and offs[-1] % 128 != 0
+        assert np.array_equal(big[:k].view(np.uint32), mid.view(np.uint32))
+    finally:
+        e.Close()
+    ref = _oracle_embed(model_path(spec), ids, offs)
+    assert_parity(big, ref)
+
+
 def test_config2_full_batch_properties(model_path):
     """The full configs[2] batch (256 sequences): unit norms, run-to-run
     bit-identical, and oracle parity of a sample of its sequences."""
