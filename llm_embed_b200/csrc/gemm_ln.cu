@@ -37,6 +37,7 @@
 // DE_TIMEOUT; after any device error the host returns part to the marker.
 #include <cudaTypedefs.h>
 
+#include <cstdlib>
 #include <mutex>
 
 #include "gemm_epi_tc.cuh"
@@ -283,8 +284,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
       if (tile >= total) return;
       if (lane == 0) {
         const int b = q % NHIN;
-        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // after the warp's reads of buffer b
-        mbar_expect_tx(hfull(e, b), BLK);
+        mbar_expect_tx(hfull(e, b), BLK);  // the warp's reads of buffer b are complete
         tma_load_2d(hin + b * BLK, &tmap_h, col_of(tile) + (q & 3) * 32, row_of(tile), hfull(e, b));
       }
       hk = q + 1;
@@ -553,7 +553,15 @@ static cudaError_t launch_layout(const CUtensorMap& amap, const CUtensorMap& bma
   cfg.dynamicSmemBytes = L::ALLOC;
   cfg.stream = s;
   cfg.attrs = attr;
-  cfg.numAttrs = 2;
+  // LLMEMBED_LN_NONCOOPERATIVE=1 drops the cooperative attribute, for
+  // profilers that cannot replay cooperative cluster launches (Nsight
+  // Compute); the grid still fits the GPU, so on an otherwise idle GPU all
+  // pairs are resident all the same.
+  static const bool noncoop = [] {
+    const char* v = std::getenv("LLMEMBED_LN_NONCOOPERATIVE");
+    return v && v[0] == '1';
+  }();
+  cfg.numAttrs = noncoop ? 1 : 2;
   return cudaLaunchKernelEx(&cfg, gemm_ln_kernel<L>, amap, bmap, hmap, omap, K, M, m_tiles, h, ln_w, ln_b, eps, part,
                             part_rows, ctl, status);
 }
