@@ -10,10 +10,12 @@
 // Tensor-core math: mma.sync m16n8k16 (fp16 in, fp32 accumulate), operand
 // fragments loaded with ldmatrix.
 //
-//   attention_short_kernel  L <= 128: one CTA of 4 warps per (64 queries,
-//       head, sequence) keeps K, V of the whole sequence and its Q rows in
-//       shared memory (cp.async); each warp holds its 16 query rows' scores
-//       for all keys in registers (one pass).
+//   attention_short_kernel  L <= 128: one CTA of 8 warps per (sequence,
+//       head) stages Q and K, then V, of the whole sequence in shared memory
+//       (cp.async, two groups); each warp takes 16 query rows, finds their
+//       maxima while V lands, then recomputes the scores chunk by chunk for
+//       the exponentials and P.V (no score kept: 80 registers, 3 CTAs per
+//       SM).
 //   Longer sequences run the tcgen05 kernel of attention_tc.cu.
 #include <math.h>
 
@@ -31,7 +33,7 @@ using namespace attn;
 
 constexpr int SH_MAXL = 128;
 static_assert(ATTN_SHORT_MAX <= SH_MAXL, "short-kernel length class");
-constexpr int SH_QROWS = 64;
+constexpr int SH_QROWS = 128;
 constexpr int SH_WARPS = SH_QROWS / 16;
 constexpr int SH_SMEM = (SH_QROWS + 2 * SH_MAXL) * LDS * 2;
 
@@ -51,13 +53,13 @@ __device__ __forceinline__ void load_rows_async(__half (*dst)[LDS], const __half
 
 }  // namespace
 
-__global__ void __launch_bounds__(SH_WARPS * 32, 4) attention_short_kernel(const __half* __restrict__ qkv,
+__global__ void __launch_bounds__(SH_WARPS * 32, 3) attention_short_kernel(const __half* __restrict__ qkv,
                                                                        const int32_t* __restrict__ offsets, int H,
                                                                        __half* __restrict__ out) {
-  const int qb = blockIdx.x, head = blockIdx.y, s = blockIdx.z;
+  const int head = blockIdx.y, s = blockIdx.x;
   const int t0 = offsets[s];
   const int L = offsets[s + 1] - t0;
-  if (L == 0 || L > ATTN_SHORT_MAX || qb * SH_QROWS >= L) return;
+  if (L == 0 || L > ATTN_SHORT_MAX) return;
   extern __shared__ __align__(16) uint8_t smem_attn[];
   __half(*sQ)[LDS] = reinterpret_cast<__half(*)[LDS]>(smem_attn);
   __half(*sK)[LDS] = sQ + SH_QROWS;
@@ -65,15 +67,22 @@ __global__ void __launch_bounds__(SH_WARPS * 32, 4) attention_short_kernel(const
   const long ld = 3L * H;
   const __half* base = qkv + (long)t0 * ld + head * HD;
   const int Lp = (L + 15) & ~15;
-  load_rows_async(sQ, base, ld, qb * SH_QROWS, SH_QROWS, L);
+  // Q and K first, V second: the maxima pass runs while V lands.
+  load_rows_async(sQ, base, ld, 0, Lp, L);
   load_rows_async(sK, base + H, ld, 0, Lp, L);
+  asm volatile("cp.async.commit_group;" ::: "memory");
   load_rows_async(sV, base + 2 * H, ld, 0, Lp, L);
-  asm volatile("cp.async.wait_all;" ::: "memory");
+  asm volatile("cp.async.commit_group;" ::: "memory");
+  asm volatile("cp.async.wait_group 1;" ::: "memory");
   __syncthreads();
   const int warp = threadIdx.x >> 5;
-  const int qrow0 = qb * SH_QROWS + warp * 16;
+  const int qrow0 = warp * 16;
+  AttnRows r;
+  if (qrow0 < L) attn_max(r, sQ, warp * 16, sK, L);
+  asm volatile("cp.async.wait_group 0;" ::: "memory");
+  __syncthreads();
   if (qrow0 >= L) return;
-  attn_rows16<SH_MAXL>(sQ, warp * 16, sK, sV, L, out + (long)t0 * H + head * HD, H, qrow0);
+  attn_pv(r, sK, sV, L, out + (long)t0 * H + head * HD, H, qrow0);
 }
 
 cudaError_t launch_attention(const __half* qkv, const int32_t* offsets, int nseq, int max_len, int H, int heads,
@@ -95,12 +104,7 @@ cudaError_t launch_attention(const __half* qkv, const int32_t* offsets, int nseq
       if (dev < 64) attr_set |= 1ull << dev;
     }
   }
-  for (int s0 = 0; s0 < nseq; s0 += 65535) {  // grid.y/z limit
-    const int n = nseq - s0 < 65535 ? nseq - s0 : 65535;
-    const int sq = (max_len < SH_MAXL ? max_len : SH_MAXL);
-    attention_short_kernel<<<dim3((sq + SH_QROWS - 1) / SH_QROWS, heads, n), SH_WARPS * 32, SH_SMEM, s>>>(
-        qkv, offsets + s0, H, out);
-  }
+  attention_short_kernel<<<dim3(nseq, heads), SH_WARPS * 32, SH_SMEM, s>>>(qkv, offsets, H, out);
   return cudaGetLastError();
 }
 

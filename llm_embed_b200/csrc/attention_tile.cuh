@@ -67,8 +67,10 @@ __device__ __forceinline__ void pv_chunk(float (*o)[4], const uint32_t* pa, __ha
   }
 }
 
-// exp rule of ops_simd.go:70-82 on a score x already reduced by the max.
-__device__ __forceinline__ float ref_exp(float x) { return x < -10.f ? 0.f : expf(x); }
+// exp rule of ops_simd.go:70-82 on a score x already reduced by the max
+// (__expf, the hardware exponential: a few ulp from expf, far inside the
+// fp16 rounding of P that follows).
+__device__ __forceinline__ float ref_exp(float x) { return x < -10.f ? 0.f : __expf(x); }
 
 // Normalise and store 16 rows x 64 dims (rows q0 and q0+8 of this lane).
 __device__ __forceinline__ void store_rows(__half* out, long ldo, int L, int q0, float (*o)[4], float l0, float l1) {
@@ -83,77 +85,93 @@ __device__ __forceinline__ void store_rows(__half* out, long ldo, int L, int q0,
   }
 }
 
-// One warp: the 16 query rows qrow_local .. +15 of sQ (query indices
-// qrow0 .. qrow0+15 of a sequence of L <= MAXL tokens) against keys and
-// values sK, sV (rows 0 .. round_up(L, 16) - 1, zero past L); writes rows
-// q < L of the head's output block `out` (row stride ldo).  For a given L
-// the result does not depend on MAXL: masked scores are -inf, their weights
-// exactly 0, and the tiles past L are skipped.
-template <int MAXL>
-__device__ __forceinline__ void attn_rows16(__half (*sQ)[LDS], int qrow_local, __half (*sK)[LDS], __half (*sV)[LDS],
-                                            int L, __half* out, long ldo, int qrow0) {
-  const int lane = threadIdx.x & 31, g = lane >> 2, tq = lane & 3;
-  const int Lp = (L + 15) & ~15;
-  uint32_t qa[4][4];
-  load_q_frags(qa, sQ, qrow_local);
+// One warp's 16 query rows, in two passes over the keys so that no score
+// is kept: pass 1 (attn_max) finds each row's maximum tile by tile; pass 2
+// (attn_pv) recomputes each 16-key chunk's scores, exponentiates them and
+// multiplies by V.  Rows qrow_local .. +15 of sQ are query indices
+// qrow0 .. qrow0+15 of a sequence of L tokens; sK and sV hold rows
+// 0 .. round_up(L, 16) - 1 (zero past L).  Tiles at or past round_up(L, 16)
+// hold only masked keys (weight exactly 0) and are skipped, so the result
+// depends only on L.  pass 2 needs sV; pass 1 does not.
+struct AttnRows {
+  uint32_t qa[4][4];  // Q fragments (16 rows x 64 dims)
+  float mx0, mx1;     // maxima of rows g and g + 8 of this lane
+};
 
-  float sc[MAXL / 8][4];
+// Scores of keys n*8 .. n*8+7 for the warp's rows, scaled by 0.125, -inf
+// past L.
+__device__ __forceinline__ void attn_scores(float* s, const AttnRows& r, __half (*sK)[LDS], int n, int L) {
+  s[0] = s[1] = s[2] = s[3] = 0.f;
+  qk_tile(s, const_cast<uint32_t(*)[4]>(r.qa), sK, n * 8);
+  if (n * 8 + 8 <= L) {  // warp-uniform: no masked key in this tile
 #pragma unroll
-  for (int n = 0; n < MAXL / 8; n++) {
-    sc[n][0] = sc[n][1] = sc[n][2] = sc[n][3] = 0.f;
-    if (n * 8 < Lp) qk_tile(sc[n], qa, sK, n * 8);
+    for (int j = 0; j < 4; j++) s[j] *= 0.125f;
+  } else {
+    const int key = n * 8 + (threadIdx.x & 3) * 2;
+#pragma unroll
+    for (int j = 0; j < 4; j++) s[j] = (key + (j & 1) < L) ? s[j] * 0.125f : -INFINITY;
   }
-  // Tiles at or past Lp hold only masked keys: their weights are exactly 0,
-  // so skipping them leaves the maxima, the sums and O unchanged.
+}
+
+__device__ __forceinline__ void attn_max(AttnRows& r, __half (*sQ)[LDS], int qrow_local, __half (*sK)[LDS], int L) {
+  load_q_frags(r.qa, sQ, qrow_local);
+  const int Lp = (L + 15) & ~15;
   float mx0 = -INFINITY, mx1 = -INFINITY;
-#pragma unroll
-  for (int n = 0; n < MAXL / 8; n++) {
-    if (n * 8 < Lp) {
-      const int key = n * 8 + tq * 2;
-#pragma unroll
-      for (int j = 0; j < 4; j++) {
-        const float v = (key + (j & 1) < L) ? sc[n][j] * 0.125f : -INFINITY;
-        sc[n][j] = v;
-        if (j < 2) mx0 = fmaxf(mx0, v);
-        else mx1 = fmaxf(mx1, v);
-      }
-    }
+#pragma unroll 2
+  for (int n = 0; n < Lp / 8; n++) {
+    float s[4];
+    attn_scores(s, r, sK, n, L);
+    mx0 = fmaxf(mx0, fmaxf(s[0], s[1]));
+    mx1 = fmaxf(mx1, fmaxf(s[2], s[3]));
   }
 #pragma unroll
   for (int o = 1; o <= 2; o <<= 1) {
     mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, o));
     mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, o));
   }
+  r.mx0 = mx0;
+  r.mx1 = mx1;
+}
+
+// Writes rows q < L of the head's output block `out` (row stride ldo).
+__device__ __forceinline__ void attn_pv(const AttnRows& r, __half (*sK)[LDS], __half (*sV)[LDS], int L, __half* out,
+                                        long ldo, int qrow0) {
+  const int Lp = (L + 15) & ~15;
   float l0 = 0.f, l1 = 0.f;
+  float acc[8][4];
 #pragma unroll
-  for (int n = 0; n < MAXL / 8; n++) {
-    if (n * 8 < Lp) {
-      sc[n][0] = ref_exp(__fsub_rn(sc[n][0], mx0));
-      sc[n][1] = ref_exp(__fsub_rn(sc[n][1], mx0));
-      sc[n][2] = ref_exp(__fsub_rn(sc[n][2], mx1));
-      sc[n][3] = ref_exp(__fsub_rn(sc[n][3], mx1));
-      l0 += sc[n][0] + sc[n][1];
-      l1 += sc[n][2] + sc[n][3];
+  for (int i = 0; i < 8; i++) acc[i][0] = acc[i][1] = acc[i][2] = acc[i][3] = 0.f;
+#pragma unroll 1
+  for (int c = 0; c < Lp / 16; c++) {
+    float s[2][4];
+#pragma unroll
+    for (int h = 0; h < 2; h++) {
+      attn_scores(s[h], r, sK, 2 * c + h, L);
+      s[h][0] = ref_exp(__fsub_rn(s[h][0], r.mx0));
+      s[h][1] = ref_exp(__fsub_rn(s[h][1], r.mx0));
+      s[h][2] = ref_exp(__fsub_rn(s[h][2], r.mx1));
+      s[h][3] = ref_exp(__fsub_rn(s[h][3], r.mx1));
+      l0 += s[h][0] + s[h][1];
+      l1 += s[h][2] + s[h][3];
     }
+    const uint32_t pa[4] = {pack_half2(s[0][0], s[0][1]), pack_half2(s[0][2], s[0][3]), pack_half2(s[1][0], s[1][1]),
+                            pack_half2(s[1][2], s[1][3])};
+    pv_chunk(acc, pa, sV, c * 16);
   }
 #pragma unroll
   for (int o = 1; o <= 2; o <<= 1) {
     l0 += __shfl_xor_sync(0xffffffffu, l0, o);
     l1 += __shfl_xor_sync(0xffffffffu, l1, o);
   }
-  float acc[8][4];
-#pragma unroll
-  for (int i = 0; i < 8; i++) acc[i][0] = acc[i][1] = acc[i][2] = acc[i][3] = 0.f;
-#pragma unroll
-  for (int c = 0; c < MAXL / 16; c++) {
-    if (c * 16 < Lp) {
-      const uint32_t pa[4] = {pack_half2(sc[2 * c][0], sc[2 * c][1]), pack_half2(sc[2 * c][2], sc[2 * c][3]),
-                              pack_half2(sc[2 * c + 1][0], sc[2 * c + 1][1]),
-                              pack_half2(sc[2 * c + 1][2], sc[2 * c + 1][3])};
-      pv_chunk(acc, pa, sV, c * 16);
-    }
-  }
-  store_rows(out, ldo, L, qrow0 + g, acc, l0, l1);
+  store_rows(out, ldo, L, qrow0 + ((threadIdx.x & 31) >> 2), acc, l0, l1);
+}
+
+// Both passes, for callers that have K and V in shared memory already.
+__device__ __forceinline__ void attn_rows16(__half (*sQ)[LDS], int qrow_local, __half (*sK)[LDS], __half (*sV)[LDS],
+                                            int L, __half* out, long ldo, int qrow0) {
+  AttnRows r;
+  attn_max(r, sQ, qrow_local, sK, L);
+  attn_pv(r, sK, sV, L, out, ldo, qrow0);
 }
 
 }  // namespace attn

@@ -329,7 +329,7 @@ __device__ void attention_step(const SmallParams& p, uint8_t* att_smem) {
       *reinterpret_cast<uint4*>(&sQ[which * 16 + r][c]) = v;
     }
     __syncwarp();
-    attn::attn_rows16<16>(sQ, 0, sK, sV, L, p.att + (long)t0 * H + head * HD, H, 0);
+    attn::attn_rows16(sQ, 0, sK, sV, L, p.att + (long)t0 * H + head * HD, H, 0);
     __syncwarp();
   }
 }
