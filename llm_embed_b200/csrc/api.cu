@@ -442,7 +442,13 @@ static int forward(le_model* m, const int32_t* d_ids, const int32_t* d_offsets, 
       e.head_dim = m->head_dim;
       e.rope_cols = 2 * H;
       TRY(gemm(m, 0, L.qkv, hA, H, e, s));
-      PLAUNCH(4, launch_attention(qkv, d_offsets, nseq, max_len, H, m->hp.heads, m->head_dim, att, s));
+      // Batches whose GEMMs run on tensor cores also run the short
+      // sequences' attention on them; small batches keep the mma.sync tile
+      // (the same bits as the single-kernel forward).
+      if (T >= TC_MIN_M && m->head_dim == 64)
+        PLAUNCH(4, launch_attention_stc(qkv, d_offsets, nseq, T, H, m->hp.heads, att, m->status.as<DevStatus>(), s));
+      else
+        PLAUNCH(4, launch_attention(qkv, d_offsets, nseq, max_len, H, m->hp.heads, m->head_dim, att, s));
       if (max_len > ATTN_SHORT_MAX)
         PLAUNCH(4, launch_attention_tc(qkv, d_offsets, nseq, T, max_len, ATTN_SHORT_MAX + 1, H, m->hp.heads, att,
                                        m->status.as<DevStatus>(), s));

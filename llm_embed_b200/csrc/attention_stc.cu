@@ -1,0 +1,351 @@
+// Tensor-core (tcgen05) attention for sequences of at most 128 tokens in
+// large batches (bert.go:356-402): the workload of the batched configs,
+// where every (sequence, head) is one small unit of work.
+//
+// Persistent kernel, one CTA per SM, walking (sequence, head) units with G=4
+// units in flight.  A unit's whole key range fits one MMA: S = Q.K^T (M=128
+// query rows, N=L rounded up to 16, K=64) into the unit's 128-column TMEM
+// slot; a softmax group (4 warps, thread = query row) reads its row of S,
+// finds the exact maximum and writes P = exp(0.125 S - max) (0 when more
+// than 10 below the maximum, the reference's rule, ops_simd.go:70-82) as
+// fp16 over the unit's Q and K in shared memory (the S MMA has read them);
+// O = P.V (N=64, K=L rounded up to 16) then lands in the first 64 columns of
+// the same TMEM slot, and the group normalises and stores it.
+//
+//   warp 0      producer: TMA loads of Q (128 rows), K and V (L rounded up to
+//               64 rows) of a unit into one of G stages.
+//   warp 1      TMEM allocation (G slots); one lane issues S(i), then
+//               P(i-3).V(i-3), so every group can hold a unit.
+//   warps 2-17  G softmax groups; group g takes the units i = g mod G.
+//
+// Operands as in attention_tc.cu: one TMA map over qkv [T][3H] (64-column
+// boxes of 64 rows, 128-byte swizzle); Q and K K-major; V [keys][64] the
+// MN-major B operand of P.V (16 keys = 2048 bytes); P [128][keys] K-major in
+// 64-key swizzled blocks.  Rows past the sequence belong to the next one (or
+// are zero past T): their scores are masked and their outputs not stored.
+// Every wait is bounded (WAIT_LIMIT_NS) and reports DE_TIMEOUT.
+#include <cudaTypedefs.h>
+
+#include <mutex>
+
+#include "kernels.h"
+#include "tcgen05.cuh"
+
+namespace le {
+namespace stc {
+
+using namespace tcx;
+
+constexpr int BQ = 128;  // query rows per unit (TMEM lanes)
+constexpr int MAXL = 128;
+static_assert(MAXL == ATTN_SHORT_MAX, "this kernel covers the short-sequence class");
+constexpr int HD = 64;
+constexpr int BOX = 64;   // rows per TMA box
+constexpr int G = 4;      // units in flight: stages, TMEM slots, softmax groups
+constexpr int GROUP_WARPS = 4;  // one query row per thread
+constexpr int SOFT_WARP0 = 2;
+constexpr int NTHREADS = (SOFT_WARP0 + G * GROUP_WARPS) * 32;
+constexpr int QKV_BYTES = MAXL * HD * 2;  // 16 KB: 128 rows of one of Q, K, V
+constexpr int STAGE_BYTES = 3 * QKV_BYTES;  // Q | K (then P) | V
+constexpr int TMEM_COLS = 512;              // G slots of 128 columns: S, then O in its first 64
+
+struct Lay {
+  static constexpr int OFF_ST = 0;  // [G] stages
+  static constexpr int OFF_BAR = OFF_ST + G * STAGE_BYTES;
+  // ld_full, ld_empty, s_full, p_full, o_full, t_empty; G of each
+  static constexpr int NBAR = 6 * G;
+  static constexpr int OFF_MISC = OFF_BAR + NBAR * 8;
+  static constexpr int BYTES = OFF_MISC + 16;
+  static constexpr int ALLOC = BYTES + 1024;
+  static_assert(ALLOC <= 232448, "shared memory budget");
+};
+
+__device__ __forceinline__ void tmem_ld32_nowait(uint32_t taddr, uint32_t* r) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,%18,%19,%"
+      "20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
+        "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]),
+        "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]),
+        "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
+}
+__device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+
+// Unit u -> (sequence, head); its length (0 when the unit is not this
+// kernel's: empty or longer than MAXL).
+__device__ __forceinline__ int unit_len(const int32_t* offsets, int heads, int u, int* t0, int* head) {
+  const int s = u / heads;
+  *head = u - s * heads;
+  *t0 = offsets[s];
+  const int L = offsets[s + 1] - *t0;
+  return L > MAXL ? 0 : L;
+}
+
+// The CTA's i-th unit of work (units of length 0 skipped): its unit index,
+// or -1 past the end.  Every role walks the same sequence.
+struct UnitWalk {
+  const int32_t* offsets;
+  int heads, nunits, u;
+  __device__ int next(int* t0, int* head, int* L) {
+    for (; u < nunits; u += gridDim.x) {
+      *L = unit_len(offsets, heads, u, t0, head);
+      if (*L > 0) {
+        const int r = u;
+        u += gridDim.x;
+        return r;
+      }
+    }
+    return -1;
+  }
+};
+
+__global__ void __launch_bounds__(NTHREADS, 1)
+    attention_stc_kernel(const __grid_constant__ CUtensorMap tmap, const int32_t* __restrict__ offsets, int nunits,
+                         int heads, int H, __half* __restrict__ out, DevStatus* status) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
+  const uint32_t sbase = smem_u32(smem);
+  const uint32_t bar0 = sbase + Lay::OFF_BAR;
+  auto ld_full = [&](int b) { return bar0 + 8 * b; };
+  auto ld_empty = [&](int b) { return bar0 + 8 * (G + b); };
+  auto s_full = [&](int b) { return bar0 + 8 * (2 * G + b); };
+  auto p_full = [&](int b) { return bar0 + 8 * (3 * G + b); };
+  auto o_full = [&](int b) { return bar0 + 8 * (4 * G + b); };
+  auto t_empty = [&](int b) { return bar0 + 8 * (5 * G + b); };
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + Lay::OFF_MISC);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + Lay::OFF_MISC + 4);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+
+  if (threadIdx.x == 0) {
+    *abort_flag = 0;
+    for (int b = 0; b < G; b++) {
+      mbar_init(ld_full(b), 1);
+      mbar_init(ld_empty(b), 1);
+      mbar_init(s_full(b), 1);
+      mbar_init(p_full(b), GROUP_WARPS);
+      mbar_init(o_full(b), 1);
+      mbar_init(t_empty(b), GROUP_WARPS);
+    }
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                 "r"(TMEM_COLS));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  UnitWalk walk{offsets, heads, nunits, (int)blockIdx.x};
+
+  if (warp == 0) {
+    // ---------------------------------------------------------------- producer
+    if (lane == 0) {
+      asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmap)) : "memory");
+      int t0, head, L;
+      for (int i = 0; walk.next(&t0, &head, &L) >= 0; i++) {
+        const int b = i % G;
+        if (!mbar_wait_sleep(ld_empty(b), ((i / G) & 1) ^ 1, abort_flag, status, 81)) break;
+        const int nbox = (L + BOX - 1) / BOX;
+        const uint32_t st = sbase + Lay::OFF_ST + b * STAGE_BYTES;
+        mbar_expect_tx(ld_full(b), QKV_BYTES + nbox * 2 * (BOX * HD * 2));
+        for (int x = 0; x < 2; x++) tma_load_2d(st + x * BOX * 128, &tmap, head * HD, t0 + x * BOX, ld_full(b));
+        for (int x = 0; x < nbox; x++) {
+          tma_load_2d(st + QKV_BYTES + x * BOX * 128, &tmap, H + head * HD, t0 + x * BOX, ld_full(b));
+          tma_load_2d(st + 2 * QKV_BYTES + x * BOX * 128, &tmap, 2 * H + head * HD, t0 + x * BOX, ld_full(b));
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ---------------------------------------------------------------- MMA
+    if (lane == 0) {
+      bool ok = true;
+      int np_of[G] = {};
+      // O(j) = P(j).V(j) into the first 64 columns of unit j's TMEM slot
+      // (its scores are consumed once P is written).
+      auto issue_pv = [&](int j) -> bool {
+        const int b = j % G;
+        if (!mbar_wait_sleep(p_full(b), (j / G) & 1, abort_flag, status, 82)) return false;
+        tc_fence_after();
+        const uint32_t paddr = sbase + Lay::OFF_ST + b * STAGE_BYTES;  // P over Q | K
+        const uint32_t vaddr = paddr + 2 * QKV_BYTES;
+        const uint32_t idesc = idesc_f16(BQ, HD) | (1u << 16);  // B (V) MN-major
+        for (int kk = 0; kk < np_of[b] / 16; kk++)
+          mma_f16(tmem + b * MAXL, sw128_desc(paddr + (kk >> 2) * QKV_BYTES + (kk & 3) * 32),
+                  sw128_desc(vaddr + kk * 2048), idesc, kk != 0);
+        mma_commit(o_full(b));
+        mma_commit(ld_empty(b));  // the stage's V (and P) are read
+        return true;
+      };
+      // S(i) is issued G-1 units ahead of P(i).V(i), so every softmax
+      // group can have a unit.
+      int t0, head, L, i = 0;
+      for (; ok && walk.next(&t0, &head, &L) >= 0; i++) {
+        const int b = i % G;
+        const int np = (L + 15) & ~15;
+        // S(i) = Q . K^T once the stage has landed and the slot's previous
+        // output has been read.
+        ok = mbar_wait_sleep(ld_full(b), (i / G) & 1, abort_flag, status, 84) &&
+             mbar_wait_sleep(t_empty(b), ((i / G) & 1) ^ 1, abort_flag, status, 85);
+        if (!ok) break;
+        tc_fence_after();
+        np_of[b] = np;
+        const uint32_t qaddr = sbase + Lay::OFF_ST + b * STAGE_BYTES;
+        const uint32_t kaddr = qaddr + QKV_BYTES;
+        const uint32_t idesc = idesc_f16(BQ, np);
+#pragma unroll
+        for (int kk = 0; kk < HD / 16; kk++)
+          mma_f16(tmem + b * MAXL, sw128_desc(qaddr + kk * 32), sw128_desc(kaddr + kk * 32), idesc, kk != 0);
+        mma_commit(s_full(b));
+        if (i >= G - 1) ok = issue_pv(i - (G - 1));
+      }
+      for (int j = i - (G - 1) < 0 ? 0 : i - (G - 1); ok && j < i; j++) ok = issue_pv(j);
+    }
+  } else {
+    // ---------------------------------------------------------------- softmax groups
+    const int grp = (warp - SOFT_WARP0) / GROUP_WARPS;
+    const int quarter = warp & 3;
+    const int row = quarter * 32 + lane;  // query row of the unit
+    const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
+    int t0, head, L;
+    for (int i = 0; walk.next(&t0, &head, &L) >= 0; i++) {
+      if (i % G != grp) continue;
+      const int b = grp;
+      const uint32_t slot = tmem + lane_off + b * MAXL;
+      if (!__all_sync(0xffffffffu, mbar_wait_sleep(s_full(b), (i / G) & 1, abort_flag, status, 87))) break;
+      tc_fence_after();
+      // Maximum of the raw scores of keys < L (scaling by 0.125 is exact),
+      // 32 keys at a time.
+      const int nch = (L + 31) >> 5;
+      float mx = -INFINITY;
+      for (int c = 0; c < nch; c++) {
+        uint32_t r[32];
+        tmem_ld32_nowait(slot + c * 32, r);
+        tmem_wait_ld();
+        const int kmax = L - c * 32;
+#pragma unroll
+        for (int k = 0; k < 32; k++)
+          if (k < kmax) mx = fmaxf(mx, __uint_as_float(r[k]));
+      }
+      mx *= 0.125f;
+      // P = exp(0.125 S - max) as fp16, 0 past L, over Q | K (read by the
+      // S MMA): K-major swizzled blocks of 64 keys; columns up to L rounded
+      // up to 16 are written.
+      uint8_t* prow = smem + Lay::OFF_ST + b * STAGE_BYTES + row * 128;
+      const int np = (L + 15) & ~15;
+      float l = 0.f;
+      for (int c = 0; c < nch; c++) {
+        uint32_t r[32];
+        tmem_ld32_nowait(slot + c * 32, r);
+        tmem_wait_ld();
+        const int kmax = L - c * 32;
+#pragma unroll
+        for (int q = 0; q < 4; q++) {  // 8-key groups of the chunk
+          const int g8 = c * 4 + q;
+          if (g8 * 8 >= np) break;
+          uint32_t w[4];
+#pragma unroll
+          for (int e = 0; e < 4; e++) {
+            const int k0 = q * 8 + 2 * e;
+            const float d0 = __fsub_rn(__uint_as_float(r[k0]) * 0.125f, mx);
+            const float d1 = __fsub_rn(__uint_as_float(r[k0 + 1]) * 0.125f, mx);
+            const float p0 = (k0 >= kmax || d0 < -10.f) ? 0.f : __expf(d0);
+            const float p1 = (k0 + 1 >= kmax || d1 < -10.f) ? 0.f : __expf(d1);
+            l += p0 + p1;
+            w[e] = pack_half2(p0, p1);
+          }
+          *reinterpret_cast<uint4*>(prow + (g8 >> 3) * QKV_BYTES + (((g8 & 7) ^ (row & 7)) << 4)) =
+              make_uint4(w[0], w[1], w[2], w[3]);
+        }
+      }
+      tc_fence_before();
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+      __syncwarp();
+      if (lane == 0) mbar_arrive(p_full(b));
+      // O / l for rows < L; then the slot is free.
+      if (!__all_sync(0xffffffffu, mbar_wait_sleep(o_full(b), (i / G) & 1, abort_flag, status, 86))) break;
+      tc_fence_after();
+      uint32_t o[64];
+      tmem_ld32_nowait(slot, o);
+      tmem_ld32_nowait(slot + 32, o + 32);
+      tmem_wait_ld();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(t_empty(b));
+      if (row < L) {
+        const float inv = 1.0f / l;
+        uint4* dst = reinterpret_cast<uint4*>(out + (long)(t0 + row) * H + head * HD);
+#pragma unroll
+        for (int c = 0; c < 8; c++)
+          dst[c] = make_uint4(pack_half2(__uint_as_float(o[8 * c]) * inv, __uint_as_float(o[8 * c + 1]) * inv),
+                              pack_half2(__uint_as_float(o[8 * c + 2]) * inv, __uint_as_float(o[8 * c + 3]) * inv),
+                              pack_half2(__uint_as_float(o[8 * c + 4]) * inv, __uint_as_float(o[8 * c + 5]) * inv),
+                              pack_half2(__uint_as_float(o[8 * c + 6]) * inv, __uint_as_float(o[8 * c + 7]) * inv));
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(TMEM_COLS));
+  }
+}
+
+static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  });
+  return fn;
+}
+
+}  // namespace stc
+
+cudaError_t launch_attention_stc(const __half* qkv, const int32_t* offsets, int nseq, int T, int H, int heads,
+                                 __half* out, DevStatus* status, cudaStream_t s) {
+  if (nseq == 0 || T == 0) return cudaSuccess;
+  if (H != heads * stc::HD) return cudaErrorInvalidValue;
+  auto enc = stc::encode_fn();
+  if (!enc) return cudaErrorNotSupported;
+  if ((3L * H * 2) % 16 || (reinterpret_cast<uintptr_t>(qkv) & 15)) return cudaErrorInvalidValue;
+  CUtensorMap map;
+  const cuuint64_t dims[2] = {(cuuint64_t)(3 * H), (cuuint64_t)T};
+  const cuuint64_t strides[1] = {(cuuint64_t)(3 * H) * 2};
+  const cuuint32_t box[2] = {stc::HD, stc::BOX};
+  const cuuint32_t estr[2] = {1, 1};
+  if (enc(&map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<__half*>(qkv), dims, strides, box, estr,
+          CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+          CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+    return cudaErrorInvalidValue;
+  static std::mutex mu;
+  static int sms[64] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev >= 64) return cudaErrorInvalidDevice;
+  {
+    std::lock_guard<std::mutex> lk(mu);
+    if (sms[dev] == 0) {
+      cudaError_t e = cudaFuncSetAttribute(stc::attention_stc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                           stc::Lay::ALLOC);
+      if (e != cudaSuccess) return e;
+      cudaDeviceGetAttribute(&sms[dev], cudaDevAttrMultiProcessorCount, dev);
+    }
+  }
+  const long nunits = (long)nseq * heads;
+  if (nunits > 0x7fffffff) return cudaErrorInvalidValue;
+  const int grid = nunits < sms[dev] ? (int)nunits : sms[dev];
+  stc::attention_stc_kernel<<<grid, stc::NTHREADS, stc::Lay::ALLOC, s>>>(map, offsets, (int)nunits, heads, H, out,
+                                                                          status);
+  return cudaGetLastError();
+}
+
+}  // namespace le

@@ -42,6 +42,37 @@ __device__ __forceinline__ bool mbar_try(uint32_t bar, uint32_t parity) {
   return ok != 0;
 }
 
+// try_wait with a suspend-time hint: the thread may sleep (up to `ns`)
+// until the phase completes instead of returning at once, so waiting warps
+// take no issue slots from working ones.
+__device__ __forceinline__ bool mbar_try_sleep(uint32_t bar, uint32_t parity, uint32_t ns) {
+  uint32_t ok;
+  asm volatile(
+      "{\n.reg .pred p;\nmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\nselp.u32 %0, 1, 0, p;\n}\n"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity), "r"(ns)
+      : "memory");
+  return ok != 0;
+}
+// mbar_wait with sleeping tries (bounded the same way; each try sleeps at
+// most 20 us).
+__device__ __forceinline__ bool mbar_wait_sleep(uint32_t bar, uint32_t parity, volatile int* abort_flag, DevStatus* st,
+                                                int site) {
+  if (mbar_try_sleep(bar, parity, 20000)) return true;
+  const uint64_t t0 = globaltimer_ns();
+  for (uint32_t i = 1;; i++) {
+    if (mbar_try_sleep(bar, parity, 20000)) return true;
+    if ((i & 15) == 0) {
+      if (*abort_flag) return false;
+      if (globaltimer_ns() - t0 > WAIT_LIMIT_NS) {
+        *abort_flag = 1;
+        report(st, DE_TIMEOUT, site, (int)blockIdx.x);
+        return false;
+      }
+    }
+  }
+}
+
 #ifdef LE_TC_WAITPROF
 // Profiling build only: clock cycles each role spends in mbarrier waits, by
 // wait site (1 producer/empty_ld, 2 MMA/tempty, 3 MMA/full_ld, 4 MMA/full_b,
