@@ -8,28 +8,31 @@
 // slot; a softmax group (4 warps, thread = query row) reads its row of S,
 // finds the exact maximum and writes P = exp(0.125 S - max) (0 when more
 // than 10 below the maximum, the reference's rule, ops_simd.go:70-82) as
-// fp16 over the unit's Q and K in shared memory (the S MMA has read them);
-// O = P.V (N=64, K=L rounded up to 16) then lands in the first 64 columns of
-// the same TMEM slot, and the group normalises and stores it.
+// fp16 pairs back into the slot over the scores it has read; O = P.V (A = P
+// from TMEM, B = V from shared memory; N=64, K=L rounded up to 16) lands in
+// the slot's upper 64 columns, and the group normalises and stores it.
+// Warps whose 32 rows all lie past the sequence skip the unit.
 //
-//   warp 0      producer: TMA loads of Q (128 rows), K and V (L rounded up to
-//               64 rows) of a unit into one of G stages.
+//   warp 0      producer: TMA loads of Q (128 rows) and K (L rounded up to 64
+//               rows) into one of 4 Q|K stages, freed as soon as the unit's
+//               scores are computed, and of V into one of 5 V stages, freed
+//               after P.V; so loads run well ahead of the MMAs.
 //   warp 1      TMEM allocation (G slots); one lane issues S(i), then
 //               P(i-3).V(i-3), so every group can hold a unit.
 //   warps 2-17  G softmax groups; group g takes the units i = g mod G.
 //
-// Operands as in attention_tc.cu: one TMA map over qkv [T][3H] (64-column
-// boxes of 64 rows, 128-byte swizzle); Q and K K-major; V [keys][64] the
-// MN-major B operand of P.V (16 keys = 2048 bytes); P [128][keys] K-major in
-// 64-key swizzled blocks.  Rows past the sequence belong to the next one (or
-// are zero past T): their scores are masked and their outputs not stored.
-// Every wait is bounded (WAIT_LIMIT_NS) and reports DE_TIMEOUT.
+// Operands: one TMA map over qkv [T][3H] (64-column boxes of 64 rows,
+// 128-byte swizzle); Q and K K-major; V [keys][64] the MN-major B operand of
+// P.V (16 keys = 2048 bytes).  Rows past the sequence belong to the next one
+// (or are zero past T): their scores are masked and their outputs not
+// stored.  Every wait is bounded (WAIT_LIMIT_NS) and reports DE_TIMEOUT;
+// waiting warps sleep in mbarrier.try_wait (suspend-time hint).
 #include <cudaTypedefs.h>
 
 #include <mutex>
 
+#include "gemm_epi_tc.cuh"
 #include "kernels.h"
-#include "tcgen05.cuh"
 
 namespace le {
 namespace stc {
@@ -40,20 +43,25 @@ constexpr int BQ = 128;  // query rows per unit (TMEM lanes)
 constexpr int MAXL = 128;
 static_assert(MAXL == ATTN_SHORT_MAX, "this kernel covers the short-sequence class");
 constexpr int HD = 64;
-constexpr int BOX = 64;   // rows per TMA box
-constexpr int G = 4;      // units in flight: stages, TMEM slots, softmax groups
+constexpr int BOX = 64;         // rows per TMA box
+constexpr int G = 4;            // units in flight: TMEM slots, softmax groups
+constexpr int NQK = 4;          // Q|K stages (free once the unit's scores are computed)
+constexpr int NV = 5;           // V stages (free once the unit's P.V is computed)
 constexpr int GROUP_WARPS = 4;  // one query row per thread
 constexpr int SOFT_WARP0 = 2;
 constexpr int NTHREADS = (SOFT_WARP0 + G * GROUP_WARPS) * 32;
 constexpr int QKV_BYTES = MAXL * HD * 2;  // 16 KB: 128 rows of one of Q, K, V
-constexpr int STAGE_BYTES = 3 * QKV_BYTES;  // Q | K (then P) | V
-constexpr int TMEM_COLS = 512;              // G slots of 128 columns: S, then O in its first 64
+constexpr int TMEM_COLS = 512;            // G slots of 128 columns
+// Within a slot: S at columns [0, 128); P (fp16 pairs) written over S at
+// [0, L/2); O at [64, 128) once S is consumed.
+constexpr int TM_O = 64;
 
 struct Lay {
-  static constexpr int OFF_ST = 0;  // [G] stages
-  static constexpr int OFF_BAR = OFF_ST + G * STAGE_BYTES;
-  // ld_full, ld_empty, s_full, p_full, o_full, t_empty; G of each
-  static constexpr int NBAR = 6 * G;
+  static constexpr int OFF_QK = 0;                              // [NQK] Q | K
+  static constexpr int OFF_V = OFF_QK + NQK * 2 * QKV_BYTES;    // [NV] V
+  static constexpr int OFF_BAR = OFF_V + NV * QKV_BYTES;
+  // qk_full, qk_empty [NQK]; v_full, v_empty [NV]; s_full, p_full, o_full, t_empty [G]
+  static constexpr int NBAR = 2 * NQK + 2 * NV + 4 * G;
   static constexpr int OFF_MISC = OFF_BAR + NBAR * 8;
   static constexpr int BYTES = OFF_MISC + 16;
   static constexpr int ALLOC = BYTES + 1024;
@@ -71,6 +79,23 @@ __device__ __forceinline__ void tmem_ld32_nowait(uint32_t taddr, uint32_t* r) {
       : "r"(taddr));
 }
 __device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+__device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t* v) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::"r"(
+          taddr),
+      "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]), "r"(v[8]), "r"(v[9]),
+      "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15])
+      : "memory");
+}
+// D (TMEM) (+)= A (TMEM: lane = row, two fp16 of K per 32-bit column) . B
+// (shared memory descriptor).
+__device__ __forceinline__ void mma_f16_ts(uint32_t tmem_d, uint32_t tmem_a, uint64_t bdesc, uint32_t idesc,
+                                           uint32_t accumulate) {
+  asm volatile(
+      "{\n.reg .pred p;\nsetp.ne.b32 p, %4, 0;\n"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n}\n" ::"r"(tmem_d),
+      "r"(tmem_a), "l"(bdesc), "r"(idesc), "r"(accumulate));
+}
 
 // Unit u -> (sequence, head); its length (0 when the unit is not this
 // kernel's: empty or longer than MAXL).
@@ -107,21 +132,29 @@ __global__ void __launch_bounds__(NTHREADS, 1)
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
   const uint32_t sbase = smem_u32(smem);
   const uint32_t bar0 = sbase + Lay::OFF_BAR;
-  auto ld_full = [&](int b) { return bar0 + 8 * b; };
-  auto ld_empty = [&](int b) { return bar0 + 8 * (G + b); };
-  auto s_full = [&](int b) { return bar0 + 8 * (2 * G + b); };
-  auto p_full = [&](int b) { return bar0 + 8 * (3 * G + b); };
-  auto o_full = [&](int b) { return bar0 + 8 * (4 * G + b); };
-  auto t_empty = [&](int b) { return bar0 + 8 * (5 * G + b); };
+  auto qk_full = [&](int b) { return bar0 + 8 * b; };
+  auto qk_empty = [&](int b) { return bar0 + 8 * (NQK + b); };
+  auto v_full = [&](int b) { return bar0 + 8 * (2 * NQK + b); };
+  auto v_empty = [&](int b) { return bar0 + 8 * (2 * NQK + NV + b); };
+  auto s_full = [&](int b) { return bar0 + 8 * (2 * NQK + 2 * NV + b); };
+  auto p_full = [&](int b) { return bar0 + 8 * (2 * NQK + 2 * NV + G + b); };
+  auto o_full = [&](int b) { return bar0 + 8 * (2 * NQK + 2 * NV + 2 * G + b); };
+  auto t_empty = [&](int b) { return bar0 + 8 * (2 * NQK + 2 * NV + 3 * G + b); };
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + Lay::OFF_MISC);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + Lay::OFF_MISC + 4);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
   if (threadIdx.x == 0) {
     *abort_flag = 0;
+    for (int b = 0; b < NQK; b++) {
+      mbar_init(qk_full(b), 1);
+      mbar_init(qk_empty(b), 1);
+    }
+    for (int b = 0; b < NV; b++) {
+      mbar_init(v_full(b), 1);
+      mbar_init(v_empty(b), 1);
+    }
     for (int b = 0; b < G; b++) {
-      mbar_init(ld_full(b), 1);
-      mbar_init(ld_empty(b), 1);
       mbar_init(s_full(b), 1);
       mbar_init(p_full(b), GROUP_WARPS);
       mbar_init(o_full(b), 1);
@@ -146,16 +179,19 @@ __global__ void __launch_bounds__(NTHREADS, 1)
       asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmap)) : "memory");
       int t0, head, L;
       for (int i = 0; walk.next(&t0, &head, &L) >= 0; i++) {
-        const int b = i % G;
-        if (!mbar_wait_sleep(ld_empty(b), ((i / G) & 1) ^ 1, abort_flag, status, 81)) break;
         const int nbox = (L + BOX - 1) / BOX;
-        const uint32_t st = sbase + Lay::OFF_ST + b * STAGE_BYTES;
-        mbar_expect_tx(ld_full(b), QKV_BYTES + nbox * 2 * (BOX * HD * 2));
-        for (int x = 0; x < 2; x++) tma_load_2d(st + x * BOX * 128, &tmap, head * HD, t0 + x * BOX, ld_full(b));
-        for (int x = 0; x < nbox; x++) {
-          tma_load_2d(st + QKV_BYTES + x * BOX * 128, &tmap, H + head * HD, t0 + x * BOX, ld_full(b));
-          tma_load_2d(st + 2 * QKV_BYTES + x * BOX * 128, &tmap, 2 * H + head * HD, t0 + x * BOX, ld_full(b));
-        }
+        const int bq = i % NQK, bv = i % NV;
+        if (!mbar_wait_sleep(qk_empty(bq), ((i / NQK) & 1) ^ 1, abort_flag, status, 81)) break;
+        const uint32_t qk = sbase + Lay::OFF_QK + bq * 2 * QKV_BYTES;
+        mbar_expect_tx(qk_full(bq), QKV_BYTES + nbox * BOX * HD * 2);
+        for (int x = 0; x < 2; x++) tma_load_2d(qk + x * BOX * 128, &tmap, head * HD, t0 + x * BOX, qk_full(bq));
+        for (int x = 0; x < nbox; x++)
+          tma_load_2d(qk + QKV_BYTES + x * BOX * 128, &tmap, H + head * HD, t0 + x * BOX, qk_full(bq));
+        if (!mbar_wait_sleep(v_empty(bv), ((i / NV) & 1) ^ 1, abort_flag, status, 82)) break;
+        const uint32_t v = sbase + Lay::OFF_V + bv * QKV_BYTES;
+        mbar_expect_tx(v_full(bv), nbox * BOX * HD * 2);
+        for (int x = 0; x < nbox; x++)
+          tma_load_2d(v + x * BOX * 128, &tmap, 2 * H + head * HD, t0 + x * BOX, v_full(bv));
       }
     }
   } else if (warp == 1) {
@@ -163,42 +199,43 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     if (lane == 0) {
       bool ok = true;
       int np_of[G] = {};
-      // O(j) = P(j).V(j) into the first 64 columns of unit j's TMEM slot
-      // (its scores are consumed once P is written).
+      // O(j) = P(j).V(j), P read from TMEM.
       auto issue_pv = [&](int j) -> bool {
-        const int b = j % G;
-        if (!mbar_wait_sleep(p_full(b), (j / G) & 1, abort_flag, status, 82)) return false;
+        const int b = j % G, bv = j % NV;
+        if (!mbar_wait_sleep(p_full(b), (j / G) & 1, abort_flag, status, 83) ||
+            !mbar_wait_sleep(v_full(bv), (j / NV) & 1, abort_flag, status, 84))
+          return false;
         tc_fence_after();
-        const uint32_t paddr = sbase + Lay::OFF_ST + b * STAGE_BYTES;  // P over Q | K
-        const uint32_t vaddr = paddr + 2 * QKV_BYTES;
+        const uint32_t vaddr = sbase + Lay::OFF_V + bv * QKV_BYTES;
         const uint32_t idesc = idesc_f16(BQ, HD) | (1u << 16);  // B (V) MN-major
+        const uint32_t slot = tmem + b * MAXL;
         for (int kk = 0; kk < np_of[b] / 16; kk++)
-          mma_f16(tmem + b * MAXL, sw128_desc(paddr + (kk >> 2) * QKV_BYTES + (kk & 3) * 32),
-                  sw128_desc(vaddr + kk * 2048), idesc, kk != 0);
+          mma_f16_ts(slot + TM_O, slot + kk * 8, sw128_desc(vaddr + kk * 2048), idesc, kk != 0);
         mma_commit(o_full(b));
-        mma_commit(ld_empty(b));  // the stage's V (and P) are read
+        mma_commit(v_empty(bv));
         return true;
       };
       // S(i) is issued G-1 units ahead of P(i).V(i), so every softmax
       // group can have a unit.
       int t0, head, L, i = 0;
       for (; ok && walk.next(&t0, &head, &L) >= 0; i++) {
-        const int b = i % G;
+        const int b = i % G, bq = i % NQK;
         const int np = (L + 15) & ~15;
-        // S(i) = Q . K^T once the stage has landed and the slot's previous
+        // S(i) = Q . K^T once Q and K have landed and the slot's previous
         // output has been read.
-        ok = mbar_wait_sleep(ld_full(b), (i / G) & 1, abort_flag, status, 84) &&
-             mbar_wait_sleep(t_empty(b), ((i / G) & 1) ^ 1, abort_flag, status, 85);
+        ok = mbar_wait_sleep(qk_full(bq), (i / NQK) & 1, abort_flag, status, 85) &&
+             mbar_wait_sleep(t_empty(b), ((i / G) & 1) ^ 1, abort_flag, status, 86);
         if (!ok) break;
         tc_fence_after();
         np_of[b] = np;
-        const uint32_t qaddr = sbase + Lay::OFF_ST + b * STAGE_BYTES;
+        const uint32_t qaddr = sbase + Lay::OFF_QK + bq * 2 * QKV_BYTES;
         const uint32_t kaddr = qaddr + QKV_BYTES;
         const uint32_t idesc = idesc_f16(BQ, np);
 #pragma unroll
         for (int kk = 0; kk < HD / 16; kk++)
           mma_f16(tmem + b * MAXL, sw128_desc(qaddr + kk * 32), sw128_desc(kaddr + kk * 32), idesc, kk != 0);
         mma_commit(s_full(b));
+        mma_commit(qk_empty(bq));  // Q and K are read
         if (i >= G - 1) ok = issue_pv(i - (G - 1));
       }
       for (int j = i - (G - 1) < 0 ? 0 : i - (G - 1); ok && j < i; j++) ok = issue_pv(j);
@@ -216,73 +253,89 @@ __global__ void __launch_bounds__(NTHREADS, 1)
       const uint32_t slot = tmem + lane_off + b * MAXL;
       if (!__all_sync(0xffffffffu, mbar_wait_sleep(s_full(b), (i / G) & 1, abort_flag, status, 87))) break;
       tc_fence_after();
-      // Maximum of the raw scores of keys < L (scaling by 0.125 is exact),
-      // 32 keys at a time.
-      const int nch = (L + 31) >> 5;
-      float mx = -INFINITY;
-      for (int c = 0; c < nch; c++) {
-        uint32_t r[32];
-        tmem_ld32_nowait(slot + c * 32, r);
-        tmem_wait_ld();
-        const int kmax = L - c * 32;
-#pragma unroll
-        for (int k = 0; k < 32; k++)
-          if (k < kmax) mx = fmaxf(mx, __uint_as_float(r[k]));
-      }
-      mx *= 0.125f;
-      // P = exp(0.125 S - max) as fp16, 0 past L, over Q | K (read by the
-      // S MMA): K-major swizzled blocks of 64 keys; columns up to L rounded
-      // up to 16 are written.
-      uint8_t* prow = smem + Lay::OFF_ST + b * STAGE_BYTES + row * 128;
-      const int np = (L + 15) & ~15;
+      // A warp whose 32 rows are all past the sequence has nothing to do:
+      // its rows of P and O are never stored (rows are independent in both
+      // MMAs).
+      const bool live = quarter * 32 < L;
       float l = 0.f;
-      for (int c = 0; c < nch; c++) {
-        uint32_t r[32];
-        tmem_ld32_nowait(slot + c * 32, r);
-        tmem_wait_ld();
-        const int kmax = L - c * 32;
+      if (live) {
+        // Maximum of the raw scores of keys < L (scaling by 0.125 is
+        // exact), 32 keys at a time.
+        const int nch = (L + 31) >> 5;
+        float mx = -INFINITY;
+        for (int c = 0; c < nch; c++) {
+          uint32_t r[32];
+          tmem_ld32_nowait(slot + c * 32, r);
+          tmem_wait_ld();
+          const int kmax = L - c * 32;
+          if (kmax >= 32) {
 #pragma unroll
-        for (int q = 0; q < 4; q++) {  // 8-key groups of the chunk
-          const int g8 = c * 4 + q;
-          if (g8 * 8 >= np) break;
-          uint32_t w[4];
+            for (int k = 0; k < 32; k++) mx = fmaxf(mx, __uint_as_float(r[k]));
+          } else {
 #pragma unroll
-          for (int e = 0; e < 4; e++) {
-            const int k0 = q * 8 + 2 * e;
-            const float d0 = __fsub_rn(__uint_as_float(r[k0]) * 0.125f, mx);
-            const float d1 = __fsub_rn(__uint_as_float(r[k0 + 1]) * 0.125f, mx);
-            const float p0 = (k0 >= kmax || d0 < -10.f) ? 0.f : __expf(d0);
-            const float p1 = (k0 + 1 >= kmax || d1 < -10.f) ? 0.f : __expf(d1);
-            l += p0 + p1;
+            for (int k = 0; k < 32; k++)
+              if (k < kmax) mx = fmaxf(mx, __uint_as_float(r[k]));
+          }
+        }
+        mx *= 0.125f;
+        // P = exp(0.125 S - max) as fp16 pairs, 0 past L, over the scores
+        // already read: keys 32c .. 32c+31 to columns 16c .. 16c+15.
+        // 0.125 S - max in one fused multiply-add (0.125 S is exact), two
+        // keys per instruction.
+        const unsigned long long eighth = f2_pack(0.125f, 0.125f), nmx = f2_pack(-mx, -mx);
+        unsigned long long lsum = f2_pack(0.f, 0.f);
+        for (int c = 0; c < nch; c++) {
+          uint32_t r[32];
+          tmem_ld32_nowait(slot + c * 32, r);
+          tmem_wait_ld();
+          const int kmax = L - c * 32;
+          uint32_t w[16];
+#pragma unroll
+          for (int e = 0; e < 16; e++) {
+            float d0, d1;
+            f2_unpack(f2_fma(f2_pack(__uint_as_float(r[2 * e]), __uint_as_float(r[2 * e + 1])), eighth, nmx), d0, d1);
+            float p0 = d0 < -10.f ? 0.f : __expf(d0);
+            float p1 = d1 < -10.f ? 0.f : __expf(d1);
+            if (kmax < 32) {  // the chunk holding key L - 1
+              p0 = 2 * e < kmax ? p0 : 0.f;
+              p1 = 2 * e + 1 < kmax ? p1 : 0.f;
+            }
+            lsum = f2_add(lsum, f2_pack(p0, p1));
             w[e] = pack_half2(p0, p1);
           }
-          *reinterpret_cast<uint4*>(prow + (g8 >> 3) * QKV_BYTES + (((g8 & 7) ^ (row & 7)) << 4)) =
-              make_uint4(w[0], w[1], w[2], w[3]);
+          tmem_st16(slot + c * 16, w);
         }
+        float l0, l1;
+        f2_unpack(lsum, l0, l1);
+        l = l0 + l1;
+        asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
       }
       tc_fence_before();
-      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
       __syncwarp();
       if (lane == 0) mbar_arrive(p_full(b));
       // O / l for rows < L; then the slot is free.
-      if (!__all_sync(0xffffffffu, mbar_wait_sleep(o_full(b), (i / G) & 1, abort_flag, status, 86))) break;
+      if (!__all_sync(0xffffffffu, mbar_wait_sleep(o_full(b), (i / G) & 1, abort_flag, status, 88))) break;
       tc_fence_after();
-      uint32_t o[64];
-      tmem_ld32_nowait(slot, o);
-      tmem_ld32_nowait(slot + 32, o + 32);
-      tmem_wait_ld();
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(t_empty(b));
-      if (row < L) {
-        const float inv = 1.0f / l;
-        uint4* dst = reinterpret_cast<uint4*>(out + (long)(t0 + row) * H + head * HD);
+      if (live) {
+        uint32_t o[64];
+        tmem_ld32_nowait(slot + TM_O, o);
+        tmem_ld32_nowait(slot + TM_O + 32, o + 32);
+        tmem_wait_ld();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(t_empty(b));
+        if (row < L) {
+          const float inv = 1.0f / l;
+          uint4* dst = reinterpret_cast<uint4*>(out + (long)(t0 + row) * H + head * HD);
 #pragma unroll
-        for (int c = 0; c < 8; c++)
-          dst[c] = make_uint4(pack_half2(__uint_as_float(o[8 * c]) * inv, __uint_as_float(o[8 * c + 1]) * inv),
-                              pack_half2(__uint_as_float(o[8 * c + 2]) * inv, __uint_as_float(o[8 * c + 3]) * inv),
-                              pack_half2(__uint_as_float(o[8 * c + 4]) * inv, __uint_as_float(o[8 * c + 5]) * inv),
-                              pack_half2(__uint_as_float(o[8 * c + 6]) * inv, __uint_as_float(o[8 * c + 7]) * inv));
+          for (int c = 0; c < 8; c++)
+            dst[c] = make_uint4(pack_half2(__uint_as_float(o[8 * c]) * inv, __uint_as_float(o[8 * c + 1]) * inv),
+                                pack_half2(__uint_as_float(o[8 * c + 2]) * inv, __uint_as_float(o[8 * c + 3]) * inv),
+                                pack_half2(__uint_as_float(o[8 * c + 4]) * inv, __uint_as_float(o[8 * c + 5]) * inv),
+                                pack_half2(__uint_as_float(o[8 * c + 6]) * inv, __uint_as_float(o[8 * c + 7]) * inv));
+        }
+      } else if (lane == 0) {
+        mbar_arrive(t_empty(b));
       }
     }
   }
