@@ -79,6 +79,54 @@ __device__ __forceinline__ void tmem_ld32_nowait(uint32_t taddr, uint32_t* r) {
       : "r"(taddr));
 }
 __device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+__device__ __forceinline__ void tmem_ld16_nowait(uint32_t taddr, uint32_t* r) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
+        "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr));
+}
+__device__ __forceinline__ void tmem_st8(uint32_t taddr, const uint32_t* v) {
+  asm volatile("tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8};" ::"r"(taddr), "r"(v[0]),
+               "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7])
+               : "memory");
+}
+__device__ __forceinline__ float max3(float a, float b, float c) {
+  float r;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+  return r;
+}
+
+// Maximum of the 16 raw scores in r (keys 16c ..) that are below L.
+__device__ __forceinline__ float chunk_max(float mx, const uint32_t* r, int kmax) {
+  if (kmax >= 16) {
+#pragma unroll
+    for (int k = 0; k < 16; k += 2) mx = max3(mx, __uint_as_float(r[k]), __uint_as_float(r[k + 1]));
+  } else {
+#pragma unroll
+    for (int k = 0; k < 16; k++)
+      if (k < kmax) mx = fmaxf(mx, __uint_as_float(r[k]));
+  }
+  return mx;
+}
+
+// P of the 16 scores in r as 8 fp16 pairs (0 past kmax), added to lsum.
+__device__ __forceinline__ void chunk_p(const uint32_t* r, int kmax, unsigned long long eighth, unsigned long long nmx,
+                                        unsigned long long& lsum, uint32_t* w) {
+#pragma unroll
+  for (int e = 0; e < 8; e++) {
+    float d0, d1;
+    f2_unpack(f2_fma(f2_pack(__uint_as_float(r[2 * e]), __uint_as_float(r[2 * e + 1])), eighth, nmx), d0, d1);
+    float p0 = d0 < -10.f ? 0.f : __expf(d0);
+    float p1 = d1 < -10.f ? 0.f : __expf(d1);
+    if (kmax < 16) {  // the chunk holding key L - 1
+      p0 = 2 * e < kmax ? p0 : 0.f;
+      p1 = 2 * e + 1 < kmax ? p1 : 0.f;
+    }
+    lsum = f2_add(lsum, f2_pack(p0, p1));
+    w[e] = pack_half2(p0, p1);
+  }
+}
 __device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t* v) {
   asm volatile(
       "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::"r"(
@@ -125,7 +173,9 @@ struct UnitWalk {
   }
 };
 
-__global__ void __launch_bounds__(NTHREADS, 1)
+// 96 registers per thread: five warps of 32 threads share an SM sub-partition's
+// 16K registers.
+__global__ void __maxnreg__(96)
     attention_stc_kernel(const __grid_constant__ CUtensorMap tmap, const int32_t* __restrict__ offsets, int nunits,
                          int heads, int H, __half* __restrict__ out, DevStatus* status) {
   extern __shared__ uint8_t smem_raw[];
@@ -260,50 +310,41 @@ __global__ void __launch_bounds__(NTHREADS, 1)
       float l = 0.f;
       if (live) {
         // Maximum of the raw scores of keys < L (scaling by 0.125 is
-        // exact), 32 keys at a time.
-        const int nch = (L + 31) >> 5;
+        // exact), 16 keys at a time, the next chunk's load in flight while
+        // one is reduced.
+        const int n16 = (L + 15) >> 4;
         float mx = -INFINITY;
-        for (int c = 0; c < nch; c++) {
-          uint32_t r[32];
-          tmem_ld32_nowait(slot + c * 32, r);
-          tmem_wait_ld();
-          const int kmax = L - c * 32;
-          if (kmax >= 32) {
+        {
+          uint32_t ra[16], rb[16];
+          tmem_ld16_nowait(slot, ra);
 #pragma unroll
-            for (int k = 0; k < 32; k++) mx = fmaxf(mx, __uint_as_float(r[k]));
-          } else {
-#pragma unroll
-            for (int k = 0; k < 32; k++)
-              if (k < kmax) mx = fmaxf(mx, __uint_as_float(r[k]));
+          for (int c = 0; c < MAXL / 16; c += 2) {
+            if (c < n16) {
+              tmem_wait_ld();
+              if (c + 1 < n16) tmem_ld16_nowait(slot + (c + 1) * 16, rb);
+              mx = chunk_max(mx, ra, L - c * 16);
+            }
+            if (c + 1 < n16) {
+              tmem_wait_ld();
+              if (c + 2 < n16) tmem_ld16_nowait(slot + (c + 2) * 16, ra);
+              mx = chunk_max(mx, rb, L - (c + 1) * 16);
+            }
           }
         }
         mx *= 0.125f;
         // P = exp(0.125 S - max) as fp16 pairs, 0 past L, over the scores
-        // already read: keys 32c .. 32c+31 to columns 16c .. 16c+15.
+        // already read: keys 16c .. 16c+15 to columns 8c .. 8c+7.
         // 0.125 S - max in one fused multiply-add (0.125 S is exact), two
         // keys per instruction.
         const unsigned long long eighth = f2_pack(0.125f, 0.125f), nmx = f2_pack(-mx, -mx);
         unsigned long long lsum = f2_pack(0.f, 0.f);
-        for (int c = 0; c < nch; c++) {
-          uint32_t r[32];
-          tmem_ld32_nowait(slot + c * 32, r);
+#pragma unroll 1
+        for (int c = 0; c < n16; c++) {
+          uint32_t r[16], w[8];
+          tmem_ld16_nowait(slot + c * 16, r);
           tmem_wait_ld();
-          const int kmax = L - c * 32;
-          uint32_t w[16];
-#pragma unroll
-          for (int e = 0; e < 16; e++) {
-            float d0, d1;
-            f2_unpack(f2_fma(f2_pack(__uint_as_float(r[2 * e]), __uint_as_float(r[2 * e + 1])), eighth, nmx), d0, d1);
-            float p0 = d0 < -10.f ? 0.f : __expf(d0);
-            float p1 = d1 < -10.f ? 0.f : __expf(d1);
-            if (kmax < 32) {  // the chunk holding key L - 1
-              p0 = 2 * e < kmax ? p0 : 0.f;
-              p1 = 2 * e + 1 < kmax ? p1 : 0.f;
-            }
-            lsum = f2_add(lsum, f2_pack(p0, p1));
-            w[e] = pack_half2(p0, p1);
-          }
-          tmem_st16(slot + c * 16, w);
+          chunk_p(r, L - c * 16, eighth, nmx, lsum, w);
+          tmem_st8(slot + c * 8, w);
         }
         float l0, l1;
         f2_unpack(lsum, l0, l1);
