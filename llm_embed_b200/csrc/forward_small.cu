@@ -84,7 +84,9 @@ __device__ bool grid_sync(unsigned* counter, unsigned k, DevStatus* st, int* fla
   __syncthreads();
   if (threadIdx.x == 0) {
     *flag = 1;
-    __threadfence();
+    // The release orders the CTA's writes (made visible to this thread by
+    // the barrier above) before the arrival; the acquire loads below order
+    // every later read after the other CTAs' arrivals.
     red_release_add(counter, 1u);
     const unsigned target = (k + 1) * gridDim.x;
     if (ld_acquire(counter) < target) {
@@ -104,7 +106,6 @@ __device__ bool grid_sync(unsigned* counter, unsigned k, DevStatus* st, int* fla
         }
       }
     }
-    __threadfence();
   }
   __syncthreads();
   return *reinterpret_cast<volatile int*>(flag) != 0;
