@@ -137,6 +137,34 @@ def test_edge_lengths(model_path):
     assert_parity(got, ref)
 
 
+@pytest.mark.parametrize("lens", [
+    [128, 129, 64, 65, 16, 1, 130, 63],            # 596 tokens: fused LayerNorm GEMMs
+    [128, 129, 1, 64],                             # 322 tokens
+    [100, 5, 3],                                   # 108 tokens: mid-size GEMMs, tcgen05 attention
+])
+def test_attention_length_classes(model_path, lens):
+    """Sequences on both sides of every attention boundary (64-key boxes,
+    the 128-token short class, the long kernel from 129) in batches that run
+    the tensor-core paths, against the oracle; and each sequence equals
+    itself in a batch of the other sequences reordered."""
+    spec = small_spec(context=512)
+    path = model_path(spec)
+    ids, offs = synth.make_ids(lens, seed=21, vocab=spec.vocab)
+    e = Embedder.Load(path)
+    try:
+        got = e.EmbedIDs(ids, offs)
+        order = list(range(len(lens)))[::-1]
+        rid = np.concatenate([ids[offs[i]:offs[i + 1]] for i in order])
+        roffs = np.concatenate([[0], np.cumsum([lens[i] for i in order])]).astype(np.int32)
+        rev = e.EmbedIDs(rid, roffs)
+    finally:
+        e.Close()
+    for k, i in enumerate(order):
+        assert np.array_equal(rev[k].view(np.uint32), got[i].view(np.uint32)), f"sequence {i}"
+    ref = _oracle_embed(path, ids, offs)
+    assert_parity(got, ref)
+
+
 def test_context_length_enforced(model_path):
     spec = small_spec(context=512, seed=12)
     path = model_path(spec)
