@@ -91,11 +91,6 @@ __device__ __forceinline__ void tmem_st8(uint32_t taddr, const uint32_t* v) {
                "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7])
                : "memory");
 }
-__device__ __forceinline__ float max3(float a, float b, float c) {
-  float r;
-  asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
-  return r;
-}
 
 // Maximum of the 16 raw scores in r (keys 16c ..) that are below L.
 __device__ __forceinline__ float chunk_max(float mx, const uint32_t* r, int kmax) {

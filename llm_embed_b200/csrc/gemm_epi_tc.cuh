@@ -84,6 +84,13 @@ __device__ __forceinline__ unsigned long long f2_fma(unsigned long long a, unsig
   return r;
 }
 
+// max(a, b, c) in one instruction (sm_100 three-input max; exact).
+__device__ __forceinline__ float max3(float a, float b, float c) {
+  float r;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+  return r;
+}
+
 // geglu() of two (gate, up) pairs, as fp16x2: the same operations in the
 // same order, two lanes per instruction (the reciprocal stays per element).
 __device__ __forceinline__ uint32_t geglu2(float v0, float v1, float u0, float u1) {
