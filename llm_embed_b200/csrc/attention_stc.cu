@@ -2,31 +2,34 @@
 // large batches (bert.go:356-402): the workload of the batched configs,
 // where every (sequence, head) is one small unit of work.
 //
-// Persistent kernel, one CTA per SM, walking (sequence, head) units with G=4
-// units in flight.  A unit's whole key range fits one MMA: S = Q.K^T (M=128
-// query rows, N=L rounded up to 16, K=64) into the unit's 128-column TMEM
-// slot; a softmax group (4 warps, thread = query row) reads its row of S,
-// finds the exact maximum and writes P = exp(0.125 S - max) (0 when more
-// than 10 below the maximum, the reference's rule, ops_simd.go:70-82) as
-// fp16 pairs back into the slot over the scores it has read; O = P.V (A = P
-// from TMEM, B = V from shared memory; N=64, K=L rounded up to 16) lands in
-// the slot's upper 64 columns, and the group normalises and stores it.
-// Warps whose 32 rows all lie past the sequence skip the unit.
+// Persistent kernel, one CTA per SM, four independent groups of four warps
+// (thread = query row = TMEM lane), each with a unit in flight in its own
+// 128-column TMEM slot.  A unit's whole key range fits one MMA: S = Q.K^T
+// (M=128 query rows, N=L rounded up to 16, K=64) into the slot; the group
+// reads its rows of S, finds the exact maximum and writes P = exp(0.125 S -
+// max) (0 when more than 10 below the maximum, the reference's rule,
+// ops_simd.go:70-82) as fp16 pairs back into the slot over the scores it has
+// read; O = P.V (A = P from TMEM, B = V from shared memory; N=64, K=L
+// rounded up to 16) lands in the slot's upper 64 columns, and the group
+// normalises and stores it.  Warps whose 32 rows all lie past the sequence
+// skip the unit's arithmetic.
 //
-//   warp 0      producer: TMA loads of Q (128 rows) and K (L rounded up to 64
-//               rows) into one of 4 Q|K stages, freed as soon as the unit's
-//               scores are computed, and of V into one of 5 V stages, freed
-//               after P.V; so loads run well ahead of the MMAs.
-//   warp 1      TMEM allocation (G slots); one lane issues S(i), then
-//               P(i-3).V(i-3), so every group can hold a unit.
-//   warps 2-17  G softmax groups; group g takes the units i = g mod G.
+// One elected thread per group (lane 0 of its first warp) takes the CTA's
+// next unit from a shared counter and issues everything asynchronous of the
+// group: the TMA loads of the next unit's Q|K (as soon as S has read the
+// current ones) and V (as soon as P.V has read the current ones), S of the
+// next unit (once the group has read O out of the slot), and P.V.  The four
+// warps meet at two named barriers per unit (P written; O read).  No group
+// ever waits for another, so a long unit holds back only its own group.
 //
 // Operands: one TMA map over qkv [T][3H] (64-column boxes of 64 rows,
 // 128-byte swizzle); Q and K K-major; V [keys][64] the MN-major B operand of
 // P.V (16 keys = 2048 bytes).  Rows past the sequence belong to the next one
 // (or are zero past T): their scores are masked and their outputs not
-// stored.  Every wait is bounded (WAIT_LIMIT_NS) and reports DE_TIMEOUT;
-// waiting warps sleep in mbarrier.try_wait (suspend-time hint).
+// stored.  Every mbarrier wait is bounded (WAIT_LIMIT_NS) and reports
+// DE_TIMEOUT; a group leaves its loop only on a decision all its threads
+// share (an OR-reduction at its named barrier), after its elected thread
+// has drained the copies and MMAs it still has in flight.
 #include <cudaTypedefs.h>
 
 #include <mutex>
@@ -44,12 +47,9 @@ constexpr int MAXL = 128;
 static_assert(MAXL == ATTN_SHORT_MAX, "this kernel covers the short-sequence class");
 constexpr int HD = 64;
 constexpr int BOX = 64;         // rows per TMA box
-constexpr int G = 4;            // units in flight: TMEM slots, softmax groups
-constexpr int NQK = 4;          // Q|K stages (free once the unit's scores are computed)
-constexpr int NV = 5;           // V stages (free once the unit's P.V is computed)
+constexpr int G = 4;            // groups = units in flight = TMEM slots
 constexpr int GROUP_WARPS = 4;  // one query row per thread
-constexpr int SOFT_WARP0 = 2;
-constexpr int NTHREADS = (SOFT_WARP0 + G * GROUP_WARPS) * 32;
+constexpr int NTHREADS = G * GROUP_WARPS * 32;
 constexpr int QKV_BYTES = MAXL * HD * 2;  // 16 KB: 128 rows of one of Q, K, V
 constexpr int TMEM_COLS = 512;            // G slots of 128 columns
 // Within a slot: S at columns [0, 128); P (fp16 pairs) written over S at
@@ -57,13 +57,12 @@ constexpr int TMEM_COLS = 512;            // G slots of 128 columns
 constexpr int TM_O = 64;
 
 struct Lay {
-  static constexpr int OFF_QK = 0;                              // [NQK] Q | K
-  static constexpr int OFF_V = OFF_QK + NQK * 2 * QKV_BYTES;    // [NV] V
-  static constexpr int OFF_BAR = OFF_V + NV * QKV_BYTES;
-  // qk_full, qk_empty [NQK]; v_full, v_empty [NV]; s_full, p_full, o_full, t_empty [G]
-  static constexpr int NBAR = 2 * NQK + 2 * NV + 4 * G;
-  static constexpr int OFF_MISC = OFF_BAR + NBAR * 8;
-  static constexpr int BYTES = OFF_MISC + 16;
+  static constexpr int GSTRIDE = 3 * QKV_BYTES;  // per group: Q, K, V
+  static constexpr int OFF_BAR = G * GSTRIDE;
+  // per group: qk_full, v_full, s_full, o_full
+  static constexpr int NBAR = 4 * G;
+  static constexpr int OFF_MISC = OFF_BAR + NBAR * 8;  // abort flag, TMEM base, unit counter, next unit [G]
+  static constexpr int BYTES = OFF_MISC + 16 + 8 * G;
   static constexpr int ALLOC = BYTES + 1024;
   static_assert(ALLOC <= 232448, "shared memory budget");
 };
@@ -92,33 +91,65 @@ __device__ __forceinline__ void tmem_st8(uint32_t taddr, const uint32_t* v) {
                : "memory");
 }
 
-// Maximum of the 16 raw scores in r (keys 16c ..) that are below L.
-__device__ __forceinline__ float chunk_max(float mx, const uint32_t* r, int kmax) {
-  if (kmax >= 16) {
+#ifndef LE_STC_PK
+#define LE_STC_PK 16
+#endif
+constexpr int PK = LE_STC_PK;  // keys per step of the P pass (one TMEM load each)
+
+// Maximum of the NK raw scores in r (keys k0 ..) that are below k0 + kmax,
+// in two interleaved chains.
+template <int NK>
+__device__ __forceinline__ void chunk_max(float& m0, float& m1, const uint32_t* r, int kmax) {
+  if (kmax >= NK) {
 #pragma unroll
-    for (int k = 0; k < 16; k += 2) mx = max3(mx, __uint_as_float(r[k]), __uint_as_float(r[k + 1]));
-  } else {
+    for (int k = 0; k < NK; k += 4) {
+      m0 = max3(m0, __uint_as_float(r[k]), __uint_as_float(r[k + 1]));
+      m1 = max3(m1, __uint_as_float(r[k + 2]), __uint_as_float(r[k + 3]));
+    }
+  } else {  // the step holding key L - 1 (columns past it are not this unit's)
 #pragma unroll
-    for (int k = 0; k < 16; k++)
-      if (k < kmax) mx = fmaxf(mx, __uint_as_float(r[k]));
+    for (int k = 0; k < NK; k += 2) {
+      m0 = fmaxf(m0, k < kmax ? __uint_as_float(r[k]) : -INFINITY);
+      m1 = fmaxf(m1, k + 1 < kmax ? __uint_as_float(r[k + 1]) : -INFINITY);
+    }
   }
-  return mx;
 }
 
-// P of the 16 scores in r as 8 fp16 pairs (0 past kmax), added to lsum.
-__device__ __forceinline__ void chunk_p(const uint32_t* r, int kmax, unsigned long long eighth, unsigned long long nmx,
-                                        unsigned long long& lsum, uint32_t* w) {
+// 2^x (the MUFU exponential, ex2.approx).
+__device__ __forceinline__ float ex2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+// exp(0.125 S - max) = 2^x with x = S * (0.125 log2 e) - max * (0.125 log2 e),
+// one fused multiply-add for two keys; the reference's cutoff (weight 0
+// when 0.125 S - max < -10, ops_simd.go:70-82) in the same base-2 units.
+constexpr float SCALE2 = 0.125f * 1.4426950408889634f;
+constexpr float CUT2 = -10.0f * 1.4426950408889634f;
+
+// P of the NK scores in r as NK/2 fp16 pairs (0 at and past kmax), their
+// sum added to two two-lane accumulators.  r is overwritten.
+template <int NK>
+__device__ __forceinline__ void chunk_p(uint32_t* r, int kmax, unsigned long long scale, unsigned long long off,
+                                        unsigned long long& s0, unsigned long long& s1, uint32_t* w) {
 #pragma unroll
-  for (int e = 0; e < 8; e++) {
-    float d0, d1;
-    f2_unpack(f2_fma(f2_pack(__uint_as_float(r[2 * e]), __uint_as_float(r[2 * e + 1])), eighth, nmx), d0, d1);
-    float p0 = d0 < -10.f ? 0.f : __expf(d0);
-    float p1 = d1 < -10.f ? 0.f : __expf(d1);
-    if (kmax < 16) {  // the chunk holding key L - 1
-      p0 = 2 * e < kmax ? p0 : 0.f;
-      p1 = 2 * e + 1 < kmax ? p1 : 0.f;
-    }
-    lsum = f2_add(lsum, f2_pack(p0, p1));
+  for (int e = 0; e < NK / 2; e++) {
+    float x0, x1;
+    f2_unpack(f2_fma(f2_pack(__uint_as_float(r[2 * e]), __uint_as_float(r[2 * e + 1])), scale, off), x0, x1);
+    r[2 * e] = __float_as_uint(x0 < CUT2 ? 0.f : ex2(x0));
+    r[2 * e + 1] = __float_as_uint(x1 < CUT2 ? 0.f : ex2(x1));
+  }
+  if (kmax < NK) {  // the step holding key L - 1
+#pragma unroll
+    for (int e = 0; e < NK; e++) r[e] = e < kmax ? r[e] : 0u;
+  }
+#pragma unroll
+  for (int e = 0; e < NK / 2; e++) {
+    const float p0 = __uint_as_float(r[2 * e]), p1 = __uint_as_float(r[2 * e + 1]);
+    if (e & 1)
+      s1 = f2_add(s1, f2_pack(p0, p1));
+    else
+      s0 = f2_add(s0, f2_pack(p0, p1));
     w[e] = pack_half2(p0, p1);
   }
 }
@@ -130,6 +161,22 @@ __device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t* v) {
       "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15])
       : "memory");
 }
+template <int N>
+__device__ __forceinline__ void tmem_ld_nowait(uint32_t taddr, uint32_t* r) {
+  static_assert(N == 16 || N == 32, "16 or 32 columns");
+  if constexpr (N == 16)
+    tmem_ld16_nowait(taddr, r);
+  else
+    tmem_ld32_nowait(taddr, r);
+}
+// N/2 columns: the fp16 pairs of N keys.
+template <int N>
+__device__ __forceinline__ void tmem_st_half(uint32_t taddr, const uint32_t* v) {
+  if constexpr (N == 16)
+    tmem_st8(taddr, v);
+  else
+    tmem_st16(taddr, v);
+}
 // D (TMEM) (+)= A (TMEM: lane = row, two fp16 of K per 32-bit column) . B
 // (shared memory descriptor).
 __device__ __forceinline__ void mma_f16_ts(uint32_t tmem_d, uint32_t tmem_a, uint64_t bdesc, uint32_t idesc,
@@ -139,7 +186,6 @@ __device__ __forceinline__ void mma_f16_ts(uint32_t tmem_d, uint32_t tmem_a, uin
       "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n}\n" ::"r"(tmem_d),
       "r"(tmem_a), "l"(bdesc), "r"(idesc), "r"(accumulate));
 }
-
 // Unit u -> (sequence, head); its length (0 when the unit is not this
 // kernel's: empty or longer than MAXL).
 __device__ __forceinline__ int unit_len(const int32_t* offsets, int heads, int u, int* t0, int* head) {
@@ -150,64 +196,51 @@ __device__ __forceinline__ int unit_len(const int32_t* offsets, int heads, int u
   return L > MAXL ? 0 : L;
 }
 
-// The CTA's i-th unit of work (units of length 0 skipped): its unit index,
-// or -1 past the end.  Every role walks the same sequence.
-struct UnitWalk {
-  const int32_t* offsets;
-  int heads, nunits, u;
-  __device__ int next(int* t0, int* head, int* L) {
-    for (; u < nunits; u += gridDim.x) {
-      *L = unit_len(offsets, heads, u, t0, head);
-      if (*L > 0) {
-        const int r = u;
-        u += gridDim.x;
-        return r;
-      }
-    }
-    return -1;
-  }
-};
+// OR of `v` over the 128 threads of named barrier `id` (all of them get
+// the same answer), with the barrier's memory ordering.
+__device__ __forceinline__ bool group_any(int id, bool v) {
+  uint32_t r;
+  asm volatile(
+      "{\n.reg .pred p, q;\nsetp.ne.u32 q, %1, 0;\nbarrier.cta.red.or.pred p, %2, 128, q;\nselp.u32 %0, 1, 0, p;\n}\n"
+      : "=r"(r)
+      : "r"((uint32_t)v), "r"(id)
+      : "memory");
+  return r != 0;
+}
 
-// 96 registers per thread: five warps of 32 threads share an SM sub-partition's
-// 16K registers.
-__global__ void __maxnreg__(96)
+// Bounded wait for a phase without the abort check: the elected thread
+// draining its own copies and MMAs before the CTA exits.
+__device__ __forceinline__ void drain(uint32_t bar, uint32_t parity) {
+  const uint64_t t0 = globaltimer_ns();
+  while (!mbar_try(bar, parity))
+    if (globaltimer_ns() - t0 > 10000000ull) break;  // 10 ms
+}
+
+// 128 registers per thread: 16 warps of 32 threads share the SM's 64K.
+__global__ void __launch_bounds__(NTHREADS, 1)
     attention_stc_kernel(const __grid_constant__ CUtensorMap tmap, const int32_t* __restrict__ offsets, int nunits,
                          int heads, int H, __half* __restrict__ out, DevStatus* status) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
   const uint32_t sbase = smem_u32(smem);
-  const uint32_t bar0 = sbase + Lay::OFF_BAR;
-  auto qk_full = [&](int b) { return bar0 + 8 * b; };
-  auto qk_empty = [&](int b) { return bar0 + 8 * (NQK + b); };
-  auto v_full = [&](int b) { return bar0 + 8 * (2 * NQK + b); };
-  auto v_empty = [&](int b) { return bar0 + 8 * (2 * NQK + NV + b); };
-  auto s_full = [&](int b) { return bar0 + 8 * (2 * NQK + 2 * NV + b); };
-  auto p_full = [&](int b) { return bar0 + 8 * (2 * NQK + 2 * NV + G + b); };
-  auto o_full = [&](int b) { return bar0 + 8 * (2 * NQK + 2 * NV + 2 * G + b); };
-  auto t_empty = [&](int b) { return bar0 + 8 * (2 * NQK + 2 * NV + 3 * G + b); };
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + Lay::OFF_MISC);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + Lay::OFF_MISC + 4);
+  int* unit_ctr = reinterpret_cast<int*>(smem + Lay::OFF_MISC + 8);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int grp = warp / GROUP_WARPS;
+  // Next unit of the group, double-buffered by unit parity: written by the
+  // elected thread while the group may still read the other entry.
+  volatile int* unit_next = reinterpret_cast<volatile int*>(smem + Lay::OFF_MISC + 16) + 2 * grp;
+  const uint32_t qk_full = sbase + Lay::OFF_BAR + 8 * (4 * grp), v_full = qk_full + 8, s_full = qk_full + 16,
+                 o_full = qk_full + 24;
 
   if (threadIdx.x == 0) {
     *abort_flag = 0;
-    for (int b = 0; b < NQK; b++) {
-      mbar_init(qk_full(b), 1);
-      mbar_init(qk_empty(b), 1);
-    }
-    for (int b = 0; b < NV; b++) {
-      mbar_init(v_full(b), 1);
-      mbar_init(v_empty(b), 1);
-    }
-    for (int b = 0; b < G; b++) {
-      mbar_init(s_full(b), 1);
-      mbar_init(p_full(b), GROUP_WARPS);
-      mbar_init(o_full(b), 1);
-      mbar_init(t_empty(b), GROUP_WARPS);
-    }
+    *unit_ctr = 0;
+    for (int b = 0; b < Lay::NBAR; b++) mbar_init(sbase + Lay::OFF_BAR + 8 * b, 1);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
-  if (warp == 1) {
+  if (warp == 0) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
                  "r"(TMEM_COLS));
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
@@ -216,169 +249,210 @@ __global__ void __maxnreg__(96)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  UnitWalk walk{offsets, heads, nunits, (int)blockIdx.x};
 
-  if (warp == 0) {
-    // ---------------------------------------------------------------- producer
-    if (lane == 0) {
-      asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmap)) : "memory");
-      int t0, head, L;
-      for (int i = 0; walk.next(&t0, &head, &L) >= 0; i++) {
-        const int nbox = (L + BOX - 1) / BOX;
-        const int bq = i % NQK, bv = i % NV;
-        if (!mbar_wait_sleep(qk_empty(bq), ((i / NQK) & 1) ^ 1, abort_flag, status, 81)) break;
-        const uint32_t qk = sbase + Lay::OFF_QK + bq * 2 * QKV_BYTES;
-        mbar_expect_tx(qk_full(bq), QKV_BYTES + nbox * BOX * HD * 2);
-        for (int x = 0; x < 2; x++) tma_load_2d(qk + x * BOX * 128, &tmap, head * HD, t0 + x * BOX, qk_full(bq));
-        for (int x = 0; x < nbox; x++)
-          tma_load_2d(qk + QKV_BYTES + x * BOX * 128, &tmap, H + head * HD, t0 + x * BOX, qk_full(bq));
-        if (!mbar_wait_sleep(v_empty(bv), ((i / NV) & 1) ^ 1, abort_flag, status, 82)) break;
-        const uint32_t v = sbase + Lay::OFF_V + bv * QKV_BYTES;
-        mbar_expect_tx(v_full(bv), nbox * BOX * HD * 2);
-        for (int x = 0; x < nbox; x++)
-          tma_load_2d(v + x * BOX * 128, &tmap, 2 * H + head * HD, t0 + x * BOX, v_full(bv));
+  const int quarter = warp & 3;         // TMEM lanes 32*quarter .. +31
+  const int row = quarter * 32 + lane;  // query row of the unit
+  const bool elect = quarter == 0 && lane == 0;
+  const int bar_id = 1 + grp;
+  const uint32_t sq = sbase + grp * Lay::GSTRIDE, sk = sq + QKV_BYTES, sv = sk + QKV_BYTES;
+  const uint32_t col = tmem + grp * MAXL;  // the group's slot
+  const uint32_t slot = col + ((uint32_t)(quarter * 32) << 16);
+
+  // Elected thread: the CTA's next unit with work for this kernel, or -1.
+  auto fetch = [&]() -> int {
+    for (;;) {
+      const long u = blockIdx.x + (long)atomicAdd(unit_ctr, 1) * gridDim.x;
+      if (u >= nunits) return -1;
+      int t0, head;
+      if (unit_len(offsets, heads, (int)u, &t0, &head) > 0) return (int)u;
+    }
+  };
+  auto load_qk = [&](int u) {
+    int t0, head;
+    const int L = unit_len(offsets, heads, u, &t0, &head), nbox = (L + BOX - 1) / BOX;
+    mbar_expect_tx(qk_full, QKV_BYTES + nbox * BOX * HD * 2);
+    for (int x = 0; x < 2; x++) tma_load_2d(sq + x * BOX * 128, &tmap, head * HD, t0 + x * BOX, qk_full);
+    for (int x = 0; x < nbox; x++) tma_load_2d(sk + x * BOX * 128, &tmap, H + head * HD, t0 + x * BOX, qk_full);
+  };
+  auto load_v = [&](int u) {
+    int t0, head;
+    const int L = unit_len(offsets, heads, u, &t0, &head), nbox = (L + BOX - 1) / BOX;
+    mbar_expect_tx(v_full, nbox * BOX * HD * 2);
+    for (int x = 0; x < nbox; x++) tma_load_2d(sv + x * BOX * 128, &tmap, 2 * H + head * HD, t0 + x * BOX, v_full);
+  };
+  // S = Q . K^T into the slot (N = L rounded up to 16).
+  auto issue_s = [&](int np) {
+    const uint32_t idesc = idesc_f16(BQ, np);
+#pragma unroll
+    for (int kk = 0; kk < HD / 16; kk++)
+      mma_f16(col, sw128_desc(sq + kk * 32), sw128_desc(sk + kk * 32), idesc, kk != 0);
+    mma_commit(s_full);
+  };
+  // O = P.V, P read from the slot's TMEM (K = L rounded up to 16).
+  auto issue_pv = [&](int np) {
+    const uint32_t idesc = idesc_f16(BQ, HD) | (1u << 16);  // B (V) MN-major
+    for (int kk = 0; kk < np / 16; kk++)
+      mma_f16_ts(col + TM_O, col + kk * 8, sw128_desc(sv + kk * 2048), idesc, kk != 0);
+    mma_commit(o_full);
+  };
+
+  // Phases issued / waited by the elected thread (for the drain on exit).
+  uint32_t nq = 0, nqw = 0, nv = 0, nvw = 0, ns = 0, no = 0;
+  bool bad = false;
+  // Elected thread: the unit after the one in flight, taken a unit ahead so
+  // that the counter and offsets loads stay off the group's critical path.
+  int ua = -1;
+  if (elect) {
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmap)) : "memory");
+    const int u = fetch();
+    unit_next[0] = u;
+    if (u >= 0) {
+      ua = fetch();
+      load_qk(u), nq++;
+      load_v(u), nv++;
+      bad = !mbar_wait_sleep(qk_full, 0, abort_flag, status, 81);
+      if (!bad) {
+        nqw++;
+        int t0, head;
+        issue_s((unit_len(offsets, heads, u, &t0, &head) + 15) & ~15), ns++;
       }
     }
-  } else if (warp == 1) {
-    // ---------------------------------------------------------------- MMA
-    if (lane == 0) {
-      bool ok = true;
-      int np_of[G] = {};
-      // O(j) = P(j).V(j), P read from TMEM.
-      auto issue_pv = [&](int j) -> bool {
-        const int b = j % G, bv = j % NV;
-        if (!mbar_wait_sleep(p_full(b), (j / G) & 1, abort_flag, status, 83) ||
-            !mbar_wait_sleep(v_full(bv), (j / NV) & 1, abort_flag, status, 84))
-          return false;
-        tc_fence_after();
-        const uint32_t vaddr = sbase + Lay::OFF_V + bv * QKV_BYTES;
-        const uint32_t idesc = idesc_f16(BQ, HD) | (1u << 16);  // B (V) MN-major
-        const uint32_t slot = tmem + b * MAXL;
-        for (int kk = 0; kk < np_of[b] / 16; kk++)
-          mma_f16_ts(slot + TM_O, slot + kk * 8, sw128_desc(vaddr + kk * 2048), idesc, kk != 0);
-        mma_commit(o_full(b));
-        mma_commit(v_empty(bv));
-        return true;
-      };
-      // S(i) is issued G-1 units ahead of P(i).V(i), so every softmax
-      // group can have a unit.
-      int t0, head, L, i = 0;
-      for (; ok && walk.next(&t0, &head, &L) >= 0; i++) {
-        const int b = i % G, bq = i % NQK;
-        const int np = (L + 15) & ~15;
-        // S(i) = Q . K^T once Q and K have landed and the slot's previous
-        // output has been read.
-        ok = mbar_wait_sleep(qk_full(bq), (i / NQK) & 1, abort_flag, status, 85) &&
-             mbar_wait_sleep(t_empty(b), ((i / G) & 1) ^ 1, abort_flag, status, 86);
-        if (!ok) break;
-        tc_fence_after();
-        np_of[b] = np;
-        const uint32_t qaddr = sbase + Lay::OFF_QK + bq * 2 * QKV_BYTES;
-        const uint32_t kaddr = qaddr + QKV_BYTES;
-        const uint32_t idesc = idesc_f16(BQ, np);
-#pragma unroll
-        for (int kk = 0; kk < HD / 16; kk++)
-          mma_f16(tmem + b * MAXL, sw128_desc(qaddr + kk * 32), sw128_desc(kaddr + kk * 32), idesc, kk != 0);
-        mma_commit(s_full(b));
-        mma_commit(qk_empty(bq));  // Q and K are read
-        if (i >= G - 1) ok = issue_pv(i - (G - 1));
-      }
-      for (int j = i - (G - 1) < 0 ? 0 : i - (G - 1); ok && j < i; j++) ok = issue_pv(j);
+  }
+  bad = group_any(bar_id, bad);
+  int u = bad ? -1 : unit_next[0];
+  uint32_t sw = 0, ow = 0;  // phases of s_full / o_full the elected thread saw
+  for (int k = 0; u >= 0; k++) {
+    int t0, head;
+    const int L = unit_len(offsets, heads, u, &t0, &head);
+    const int np = (L + 15) & ~15;
+    // A warp whose 32 rows are all past the sequence has nothing to do:
+    // its rows of P and O are never stored (rows are independent in both
+    // MMAs).
+    const bool live = quarter * 32 < L;
+    // (Only the elected thread can come here with `bad` set: a failed wait
+    // after the last barrier.  Its warp then fails as a whole.)
+    if (live || elect) {
+      const bool w = !bad && mbar_wait_sleep(s_full, k & 1, abort_flag, status, 87);
+      bad = !__all_sync(0xffffffffu, w);
+      if (elect && !bad) sw++;
     }
-  } else {
-    // ---------------------------------------------------------------- softmax groups
-    const int grp = (warp - SOFT_WARP0) / GROUP_WARPS;
-    const int quarter = warp & 3;
-    const int row = quarter * 32 + lane;  // query row of the unit
-    const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
-    int t0, head, L;
-    for (int i = 0; walk.next(&t0, &head, &L) >= 0; i++) {
-      if (i % G != grp) continue;
-      const int b = grp;
-      const uint32_t slot = tmem + lane_off + b * MAXL;
-      if (!__all_sync(0xffffffffu, mbar_wait_sleep(s_full(b), (i / G) & 1, abort_flag, status, 87))) break;
-      tc_fence_after();
-      // A warp whose 32 rows are all past the sequence has nothing to do:
-      // its rows of P and O are never stored (rows are independent in both
-      // MMAs).
-      const bool live = quarter * 32 < L;
-      float l = 0.f;
-      if (live) {
-        // Maximum of the raw scores of keys < L (scaling by 0.125 is
-        // exact), 16 keys at a time, the next chunk's load in flight while
-        // one is reduced.
-        const int n16 = (L + 15) >> 4;
-        float mx = -INFINITY;
-        {
-          uint32_t ra[16], rb[16];
-          tmem_ld16_nowait(slot, ra);
+    tc_fence_after();
+    int un = -1;
+    if (elect && !bad) {
+      // Q and K are read: the next unit's go to the same buffers.
+      un = ua;
+      unit_next[(k + 1) & 1] = un;
+      if (un >= 0) load_qk(un), nq++;
+    }
+    float l = 0.f;
+    if (live && !bad) {
+      // Maximum of the raw scores of keys < L, 16 keys per TMEM load, the
+      // next load in flight while one is reduced.
+      const int n16 = (L + 15) >> 4;
+      float m0 = -INFINITY, m1 = -INFINITY;
+      {
+        uint32_t ra[16], rb[16];
+        tmem_ld16_nowait(slot, ra);
 #pragma unroll
-          for (int c = 0; c < MAXL / 16; c += 2) {
-            if (c < n16) {
-              tmem_wait_ld();
-              if (c + 1 < n16) tmem_ld16_nowait(slot + (c + 1) * 16, rb);
-              mx = chunk_max(mx, ra, L - c * 16);
-            }
-            if (c + 1 < n16) {
-              tmem_wait_ld();
-              if (c + 2 < n16) tmem_ld16_nowait(slot + (c + 2) * 16, ra);
-              mx = chunk_max(mx, rb, L - (c + 1) * 16);
-            }
+        for (int c = 0; c < MAXL / 16; c += 2) {
+          if (c < n16) {
+            tmem_wait_ld();
+            if (c + 1 < n16) tmem_ld16_nowait(slot + (c + 1) * 16, rb);
+            chunk_max<16>(m0, m1, ra, L - c * 16);
+          }
+          if (c + 1 < n16) {
+            tmem_wait_ld();
+            if (c + 2 < n16) tmem_ld16_nowait(slot + (c + 2) * 16, ra);
+            chunk_max<16>(m0, m1, rb, L - (c + 1) * 16);
           }
         }
-        mx *= 0.125f;
-        // P = exp(0.125 S - max) as fp16 pairs, 0 past L, over the scores
-        // already read: keys 16c .. 16c+15 to columns 8c .. 8c+7.
-        // 0.125 S - max in one fused multiply-add (0.125 S is exact), two
-        // keys per instruction.
-        const unsigned long long eighth = f2_pack(0.125f, 0.125f), nmx = f2_pack(-mx, -mx);
-        unsigned long long lsum = f2_pack(0.f, 0.f);
-#pragma unroll 1
-        for (int c = 0; c < n16; c++) {
-          uint32_t r[16], w[8];
-          tmem_ld16_nowait(slot + c * 16, r);
-          tmem_wait_ld();
-          chunk_p(r, L - c * 16, eighth, nmx, lsum, w);
-          tmem_st8(slot + c * 8, w);
-        }
-        float l0, l1;
-        f2_unpack(lsum, l0, l1);
-        l = l0 + l1;
-        asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
       }
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(p_full(b));
-      // O / l for rows < L; then the slot is free.
-      if (!__all_sync(0xffffffffu, mbar_wait_sleep(o_full(b), (i / G) & 1, abort_flag, status, 88))) break;
-      tc_fence_after();
-      if (live) {
-        uint32_t o[64];
-        tmem_ld32_nowait(slot + TM_O, o);
-        tmem_ld32_nowait(slot + TM_O + 32, o + 32);
+      const float mx = fmaxf(m0, m1);
+      // P, PK keys per TMEM load, over the scores already read: keys PK c ..
+      // to columns PK/2 c ..
+      // (columns past the unit's N hold no scores of it: masked, and P.V
+      // reads only the first L/2 rounded up to 8).
+      const unsigned long long scale = f2_pack(SCALE2, SCALE2), off = f2_pack(-mx * SCALE2, -mx * SCALE2);
+      unsigned long long s0 = f2_pack(0.f, 0.f), s1 = s0;
+      const int nst = (L + PK - 1) / PK;
+#pragma unroll 1
+      for (int c = 0; c < nst; c++) {
+        uint32_t r[PK], w[PK / 2];
+        tmem_ld_nowait<PK>(slot + c * PK, r);
         tmem_wait_ld();
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(t_empty(b));
-        if (row < L) {
-          const float inv = 1.0f / l;
-          uint4* dst = reinterpret_cast<uint4*>(out + (long)(t0 + row) * H + head * HD);
-#pragma unroll
-          for (int c = 0; c < 8; c++)
-            dst[c] = make_uint4(pack_half2(__uint_as_float(o[8 * c]) * inv, __uint_as_float(o[8 * c + 1]) * inv),
-                                pack_half2(__uint_as_float(o[8 * c + 2]) * inv, __uint_as_float(o[8 * c + 3]) * inv),
-                                pack_half2(__uint_as_float(o[8 * c + 4]) * inv, __uint_as_float(o[8 * c + 5]) * inv),
-                                pack_half2(__uint_as_float(o[8 * c + 6]) * inv, __uint_as_float(o[8 * c + 7]) * inv));
-        }
-      } else if (lane == 0) {
-        mbar_arrive(t_empty(b));
+        chunk_p<PK>(r, L - c * PK, scale, off, s0, s1, w);
+        tmem_st_half<PK>(slot + c * (PK / 2), w);
+      }
+      float l0, l1;
+      f2_unpack(f2_add(s0, s1), l0, l1);
+      l = l0 + l1;
+      asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+    }
+    tc_fence_before();
+    if (group_any(bar_id, bad)) break;  // P is written
+    if (elect) {
+      tc_fence_after();
+      bad = !mbar_wait_sleep(v_full, k & 1, abort_flag, status, 84);
+      if (!bad) nvw++, issue_pv(np), no++;
+      ua = un >= 0 ? fetch() : -1;
+    }
+    if (live || elect) {
+      const bool w = !bad && mbar_wait_sleep(o_full, k & 1, abort_flag, status, 88);
+      bad = !__all_sync(0xffffffffu, w);
+      if (elect && !bad) ow++;
+    }
+    tc_fence_after();
+    // V is read: the next unit's goes to the same buffer.
+    if (elect && !bad && un >= 0) load_v(un), nv++;
+    uint32_t o[64];
+    if (live && !bad) {
+      tmem_ld32_nowait(slot + TM_O, o);
+      tmem_ld32_nowait(slot + TM_O + 32, o + 32);
+      tmem_wait_ld();
+    }
+    tc_fence_before();
+    if (group_any(bar_id, bad)) break;  // O is read: the slot is free
+    u = unit_next[(k + 1) & 1];
+    if (elect && u >= 0) {
+      // S of the next unit, overlapping this unit's stores.
+      tc_fence_after();
+      bad = !mbar_wait_sleep(qk_full, (k + 1) & 1, abort_flag, status, 81);
+      if (!bad) {
+        nqw++;
+        int t1, h1;
+        issue_s((unit_len(offsets, heads, u, &t1, &h1) + 15) & ~15), ns++;
       }
     }
+    if (live && !bad && row < L) {
+      const float inv = 1.0f / l;
+      const unsigned long long inv2 = f2_pack(inv, inv);
+      uint4* dst = reinterpret_cast<uint4*>(out + (long)(t0 + row) * H + head * HD);
+#pragma unroll
+      for (int c = 0; c < 8; c++) {
+        uint32_t h[4];
+#pragma unroll
+        for (int j = 0; j < 4; j++) {
+          float a, b;
+          f2_unpack(f2_mul(f2_pack(__uint_as_float(o[8 * c + 2 * j]), __uint_as_float(o[8 * c + 2 * j + 1])), inv2), a,
+                    b);
+          h[j] = pack_half2(a, b);
+        }
+        dst[c] = make_uint4(h[0], h[1], h[2], h[3]);
+      }
+    }
+  }
+  // Copies and MMAs this group's elected thread issued but nobody waited
+  // for (only after a failure) land before the CTA exits.
+  if (elect) {
+    if (nq > nqw) drain(qk_full, (nq - 1) & 1);
+    if (nv > nvw) drain(v_full, (nv - 1) & 1);
+    if (ns > sw) drain(s_full, (ns - 1) & 1);
+    if (no > ow) drain(o_full, (no - 1) & 1);
   }
 
   tc_fence_before();
   __syncthreads();
-  if (warp == 1) {
+  if (warp == 0) {
     tc_fence_after();
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(TMEM_COLS));
   }
