@@ -61,8 +61,9 @@ struct Lay {
   static constexpr int OFF_BAR = G * GSTRIDE;
   // per group: qk_full, v_full, s_full, o_full
   static constexpr int NBAR = 4 * G;
-  static constexpr int OFF_MISC = OFF_BAR + NBAR * 8;  // abort flag, TMEM base, unit counter, next unit [G]
-  static constexpr int BYTES = OFF_MISC + 16 + 8 * G;
+  static constexpr int OFF_MISC = OFF_BAR + NBAR * 8;  // abort flag, TMEM base, unit counter
+  static constexpr int OFF_UNITS = OFF_MISC + 16;      // next unit [G][2] (int4)
+  static constexpr int BYTES = OFF_UNITS + 16 * 2 * G;
   static constexpr int ALLOC = BYTES + 1024;
   static_assert(ALLOC <= 232448, "shared memory budget");
 };
@@ -230,7 +231,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
   const int grp = warp / GROUP_WARPS;
   // Next unit of the group, double-buffered by unit parity: written by the
   // elected thread while the group may still read the other entry.
-  volatile int* unit_next = reinterpret_cast<volatile int*>(smem + Lay::OFF_MISC + 16) + 2 * grp;
+  int4* unit_next = reinterpret_cast<int4*>(smem + Lay::OFF_UNITS) + 2 * grp;
   const uint32_t qk_full = sbase + Lay::OFF_BAR + 8 * (4 * grp), v_full = qk_full + 8, s_full = qk_full + 16,
                  o_full = qk_full + 24;
 
@@ -258,27 +259,27 @@ __global__ void __launch_bounds__(NTHREADS, 1)
   const uint32_t col = tmem + grp * MAXL;  // the group's slot
   const uint32_t slot = col + ((uint32_t)(quarter * 32) << 16);
 
-  // Elected thread: the CTA's next unit with work for this kernel, or -1.
-  auto fetch = [&]() -> int {
+  // A unit as {first token, head, length} (length 0: none).  Elected
+  // thread: the CTA's next unit with work for this kernel.
+  auto fetch = [&]() -> int4 {
     for (;;) {
       const long u = blockIdx.x + (long)atomicAdd(unit_ctr, 1) * gridDim.x;
-      if (u >= nunits) return -1;
+      if (u >= nunits) return make_int4(0, 0, 0, 0);
       int t0, head;
-      if (unit_len(offsets, heads, (int)u, &t0, &head) > 0) return (int)u;
+      const int L = unit_len(offsets, heads, (int)u, &t0, &head);
+      if (L > 0) return make_int4(t0, head, L, 0);
     }
   };
-  auto load_qk = [&](int u) {
-    int t0, head;
-    const int L = unit_len(offsets, heads, u, &t0, &head), nbox = (L + BOX - 1) / BOX;
+  auto load_qk = [&](int4 un) {
+    const int nbox = (un.z + BOX - 1) / BOX;
     mbar_expect_tx(qk_full, QKV_BYTES + nbox * BOX * HD * 2);
-    for (int x = 0; x < 2; x++) tma_load_2d(sq + x * BOX * 128, &tmap, head * HD, t0 + x * BOX, qk_full);
-    for (int x = 0; x < nbox; x++) tma_load_2d(sk + x * BOX * 128, &tmap, H + head * HD, t0 + x * BOX, qk_full);
+    for (int x = 0; x < 2; x++) tma_load_2d(sq + x * BOX * 128, &tmap, un.y * HD, un.x + x * BOX, qk_full);
+    for (int x = 0; x < nbox; x++) tma_load_2d(sk + x * BOX * 128, &tmap, H + un.y * HD, un.x + x * BOX, qk_full);
   };
-  auto load_v = [&](int u) {
-    int t0, head;
-    const int L = unit_len(offsets, heads, u, &t0, &head), nbox = (L + BOX - 1) / BOX;
+  auto load_v = [&](int4 un) {
+    const int nbox = (un.z + BOX - 1) / BOX;
     mbar_expect_tx(v_full, nbox * BOX * HD * 2);
-    for (int x = 0; x < nbox; x++) tma_load_2d(sv + x * BOX * 128, &tmap, 2 * H + head * HD, t0 + x * BOX, v_full);
+    for (int x = 0; x < nbox; x++) tma_load_2d(sv + x * BOX * 128, &tmap, 2 * H + un.y * HD, un.x + x * BOX, v_full);
   };
   // S = Q . K^T into the slot (N = L rounded up to 16).
   auto issue_s = [&](int np) {
@@ -301,29 +302,24 @@ __global__ void __launch_bounds__(NTHREADS, 1)
   bool bad = false;
   // Elected thread: the unit after the one in flight, taken a unit ahead so
   // that the counter and offsets loads stay off the group's critical path.
-  int ua = -1;
+  int4 ua = make_int4(0, 0, 0, 0);
   if (elect) {
     asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmap)) : "memory");
-    const int u = fetch();
-    unit_next[0] = u;
-    if (u >= 0) {
+    const int4 u0 = fetch();
+    unit_next[0] = u0;
+    if (u0.z > 0) {
       ua = fetch();
-      load_qk(u), nq++;
-      load_v(u), nv++;
+      load_qk(u0), nq++;
+      load_v(u0), nv++;
       bad = !mbar_wait_sleep(qk_full, 0, abort_flag, status, 81);
-      if (!bad) {
-        nqw++;
-        int t0, head;
-        issue_s((unit_len(offsets, heads, u, &t0, &head) + 15) & ~15), ns++;
-      }
+      if (!bad) nqw++, issue_s((u0.z + 15) & ~15), ns++;
     }
   }
   bad = group_any(bar_id, bad);
-  int u = bad ? -1 : unit_next[0];
+  int4 cur = bad ? make_int4(0, 0, 0, 0) : unit_next[0];
   uint32_t sw = 0, ow = 0;  // phases of s_full / o_full the elected thread saw
-  for (int k = 0; u >= 0; k++) {
-    int t0, head;
-    const int L = unit_len(offsets, heads, u, &t0, &head);
+  for (int k = 0; cur.z > 0; k++) {
+    const int t0 = cur.x, head = cur.y, L = cur.z;
     const int np = (L + 15) & ~15;
     // A warp whose 32 rows are all past the sequence has nothing to do:
     // its rows of P and O are never stored (rows are independent in both
@@ -332,17 +328,17 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     // (Only the elected thread can come here with `bad` set: a failed wait
     // after the last barrier.  Its warp then fails as a whole.)
     if (live || elect) {
-      const bool w = !bad && mbar_wait_sleep(s_full, k & 1, abort_flag, status, 87);
+      const bool w = !bad && mbar_wait(s_full, k & 1, abort_flag, status, 87);
       bad = !__all_sync(0xffffffffu, w);
       if (elect && !bad) sw++;
     }
     tc_fence_after();
-    int un = -1;
+    int4 un = make_int4(0, 0, 0, 0);
     if (elect && !bad) {
       // Q and K are read: the next unit's go to the same buffers.
       un = ua;
       unit_next[(k + 1) & 1] = un;
-      if (un >= 0) load_qk(un), nq++;
+      if (un.z > 0) load_qk(un), nq++;
     }
     float l = 0.f;
     if (live && !bad) {
@@ -394,16 +390,16 @@ __global__ void __launch_bounds__(NTHREADS, 1)
       tc_fence_after();
       bad = !mbar_wait_sleep(v_full, k & 1, abort_flag, status, 84);
       if (!bad) nvw++, issue_pv(np), no++;
-      ua = un >= 0 ? fetch() : -1;
+      ua = un.z > 0 ? fetch() : make_int4(0, 0, 0, 0);
     }
     if (live || elect) {
-      const bool w = !bad && mbar_wait_sleep(o_full, k & 1, abort_flag, status, 88);
+      const bool w = !bad && mbar_wait(o_full, k & 1, abort_flag, status, 88);
       bad = !__all_sync(0xffffffffu, w);
       if (elect && !bad) ow++;
     }
     tc_fence_after();
     // V is read: the next unit's goes to the same buffer.
-    if (elect && !bad && un >= 0) load_v(un), nv++;
+    if (elect && !bad && un.z > 0) load_v(un), nv++;
     uint32_t o[64];
     if (live && !bad) {
       tmem_ld32_nowait(slot + TM_O, o);
@@ -412,16 +408,12 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     }
     tc_fence_before();
     if (group_any(bar_id, bad)) break;  // O is read: the slot is free
-    u = unit_next[(k + 1) & 1];
-    if (elect && u >= 0) {
+    cur = unit_next[(k + 1) & 1];
+    if (elect && cur.z > 0) {
       // S of the next unit, overlapping this unit's stores.
       tc_fence_after();
       bad = !mbar_wait_sleep(qk_full, (k + 1) & 1, abort_flag, status, 81);
-      if (!bad) {
-        nqw++;
-        int t1, h1;
-        issue_s((unit_len(offsets, heads, u, &t1, &h1) + 15) & ~15), ns++;
-      }
+      if (!bad) nqw++, issue_s((cur.z + 15) & ~15), ns++;
     }
     if (live && !bad && row < L) {
       const float inv = 1.0f / l;
