@@ -92,10 +92,7 @@ __device__ __forceinline__ void tmem_st8(uint32_t taddr, const uint32_t* v) {
                : "memory");
 }
 
-#ifndef LE_STC_PK
-#define LE_STC_PK 16
-#endif
-constexpr int PK = LE_STC_PK;  // keys per step of the P pass (one TMEM load each)
+constexpr int PK = 16;  // keys per step of the P pass (one TMEM load each; 32 spills registers)
 
 // Maximum of the NK raw scores in r (keys k0 ..) that are below k0 + kmax,
 // in two interleaved chains.
