@@ -247,6 +247,8 @@ __global__ void __launch_bounds__(NTHREADS, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  pdl_wait();  // qkv and the output buffer are the previous kernels'
+  pdl_trigger();
 
   const int quarter = warp & 3;         // TMEM lanes 32*quarter .. +31
   const int row = quarter * 32 + lane;  // query row of the unit
@@ -495,9 +497,9 @@ cudaError_t launch_attention_stc(const __half* qkv, const int32_t* offsets, int 
   const long nunits = (long)nseq * heads;
   if (nunits > 0x7fffffff) return cudaErrorInvalidValue;
   const int grid = nunits < sms[dev] ? (int)nunits : sms[dev];
-  stc::attention_stc_kernel<<<grid, stc::NTHREADS, stc::Lay::ALLOC, s>>>(map, offsets, (int)nunits, heads, H, out,
-                                                                          status);
-  return cudaGetLastError();
+  cudaLaunchAttribute attr[1];
+  const cudaLaunchConfig_t cfg = pdl_config(dim3(grid), dim3(stc::NTHREADS), stc::Lay::ALLOC, s, attr);
+  return cudaLaunchKernelEx(&cfg, stc::attention_stc_kernel, map, offsets, (int)nunits, heads, H, out, status);
 }
 
 }  // namespace le

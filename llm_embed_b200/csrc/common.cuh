@@ -10,6 +10,32 @@
 
 namespace le {
 
+// Programmatic dependent launch.  Kernels of the forward pass are launched
+// with programmatic stream serialization (pdl_config) so that a kernel's
+// CTAs can be placed on SMs its predecessor has left while the predecessor
+// finishes.  Every such kernel calls pdl_wait() in every thread before its
+// first global memory access (it returns once the preceding kernel has
+// completed and its writes are visible; without the launch attribute it
+// returns at once), then pdl_trigger(), which lets the next kernel be
+// scheduled once all CTAs of this one have issued it.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
+// Launch configuration with the programmatic stream serialization attribute
+// (attr must outlive the launch call).
+inline cudaLaunchConfig_t pdl_config(dim3 grid, dim3 block, size_t smem, cudaStream_t s, cudaLaunchAttribute* attr) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cfg;
+}
+
 // GGML tensor type ids (reference internal/gguf/reader.go:46-65).
 enum GgmlType : int { T_F32 = 0, T_Q8_0 = 8, T_Q4_K = 12, T_Q5_K = 13, T_Q6_K = 14 };
 

@@ -36,6 +36,8 @@ __global__ void __launch_bounds__(256) ln_rows_kernel(const float* in, const flo
                                                       const float* __restrict__ b, float eps, int T, int H,
                                                       int vocab, DevStatus* status, float* out32,
                                                       __half* __restrict__ out16) {
+  pdl_wait();
+  pdl_trigger();
   const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
   if (warp >= T) return;
@@ -96,6 +98,8 @@ __global__ void __launch_bounds__(256) ln_rows_kernel(const float* in, const flo
 // H/4 threads per sequence; empty sequences give a zero vector.
 __global__ void pool_kernel(const float* __restrict__ h, const int32_t* __restrict__ offsets, int H, int out_dim,
                             float* __restrict__ out) {
+  pdl_wait();
+  pdl_trigger();
   const int s = blockIdx.x;
   const int t0 = offsets[s], t1 = offsets[s + 1];
   const int c = threadIdx.x * 4;
@@ -159,25 +163,28 @@ cudaError_t launch_embed_ln(const int32_t* ids, int emb_type, const uint8_t* emb
                             __half* out16, DevStatus* status, cudaStream_t s) {
   if (H % 128 || H > 128 * LN_MAXV) return cudaErrorInvalidValue;
   if (T == 0) return cudaSuccess;
-  ln_rows_kernel<true><<<(T + 7) / 8, 256, 0, s>>>(nullptr, nullptr, ids, emb_type, emb, emb_row_bytes, type0, w, b, eps, T, H,
-                                                   vocab, status, out32, out16);
-  return cudaGetLastError();
+  cudaLaunchAttribute attr[1];
+  const cudaLaunchConfig_t cfg = pdl_config(dim3((T + 7) / 8), dim3(256), 0, s, attr);
+  return cudaLaunchKernelEx(&cfg, ln_rows_kernel<true>, (const float*)nullptr, (const float*)nullptr, ids, emb_type, emb,
+                            emb_row_bytes, type0, w, b, eps, T, H, vocab, status, out32, out16);
 }
 
 cudaError_t launch_ln_add(const float* in, const float* add, const float* w, const float* b, float eps, int T, int H,
                           float* out32, __half* out16, cudaStream_t s) {
   if (H % 128 || H > 128 * LN_MAXV) return cudaErrorInvalidValue;
   if (T == 0) return cudaSuccess;
-  ln_rows_kernel<false><<<(T + 7) / 8, 256, 0, s>>>(in, add, nullptr, 0, nullptr, 0, nullptr, w, b, eps, T, H, 0,
-                                                    nullptr, out32, out16);
-  return cudaGetLastError();
+  cudaLaunchAttribute attr[1];
+  const cudaLaunchConfig_t cfg = pdl_config(dim3((T + 7) / 8), dim3(256), 0, s, attr);
+  return cudaLaunchKernelEx(&cfg, ln_rows_kernel<false>, in, add, (const int32_t*)nullptr, 0, (const uint8_t*)nullptr, 0L,
+                            (const float*)nullptr, w, b, eps, T, H, 0, (DevStatus*)nullptr, out32, out16);
 }
 
 cudaError_t launch_pool(const float* h, const int32_t* offsets, int nseq, int H, int out_dim, float* out,
                         cudaStream_t s) {
   if (nseq == 0) return cudaSuccess;
-  pool_kernel<<<nseq, H / 4, 0, s>>>(h, offsets, H, out_dim, out);
-  return cudaGetLastError();
+  cudaLaunchAttribute attr[1];
+  const cudaLaunchConfig_t cfg = pdl_config(dim3(nseq), dim3(H / 4), 0, s, attr);
+  return cudaLaunchKernelEx(&cfg, pool_kernel, h, offsets, H, out_dim, out);
 }
 
 cudaError_t launch_f32_to_f16(const float* in, long n, __half* out, cudaStream_t s) {

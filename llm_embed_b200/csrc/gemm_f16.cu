@@ -123,6 +123,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NTHREADS, 1)
   cluster_sync();  // both CTAs' barriers are initialised before any remote arrive
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  pdl_wait();  // the operands and the output buffer are the previous kernels'
+  pdl_trigger();
 
   if (warp == 0) {
     // ------------------------------------------------------------ producer
@@ -303,8 +305,9 @@ static cudaError_t launch(const __half* W16, int n_virtual, int K, const __half*
   const int n_tiles = n_virtual / PN;
   const int total = m_tiles * n_tiles;
   const int pairs = total < max_pairs[dev] ? total : max_pairs[dev];
-  gemm_f16_pair_kernel<<<2 * pairs, NTHREADS, Lay::ALLOC, s>>>(amap, bmap, omap, K, m_tiles, n_tiles, ep, status);
-  return cudaGetLastError();
+  cudaLaunchAttribute attr[1];
+  const cudaLaunchConfig_t cfg = pdl_config(dim3(2 * pairs), dim3(NTHREADS), Lay::ALLOC, s, attr);
+  return cudaLaunchKernelEx(&cfg, gemm_f16_pair_kernel, amap, bmap, omap, K, m_tiles, n_tiles, ep, status);
 }
 
 }  // namespace tcf

@@ -199,6 +199,8 @@ __global__ void __launch_bounds__(NTHREADS, 1)
   cluster_sync();  // both CTAs' barriers are initialised before any remote arrive
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  pdl_wait();  // (a no-op: this cooperative launch waits for its predecessor)
+  pdl_trigger();  // the next kernel may take the SMs this one leaves
   // This launch's half of part; the idle lanes of warps 0 and 1 return the
   // other half (the next launch's) to the marker.
   const unsigned epoch = *reinterpret_cast<volatile unsigned*>(ctl + 1);
