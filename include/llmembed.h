@@ -37,7 +37,10 @@ extern "C" {
 #define LE_ENOMEM -4   /* device or host allocation failed */
 #define LE_EIO -5      /* GGUF file could not be read or parsed */
 
-/* GGML tensor type ids accepted for weights (internal/gguf/reader.go:46-65). */
+/* GGML tensor type ids accepted for weights (internal/gguf/reader.go:46-65).
+ * Projection weights may also carry ids 15 and 16, which the reference's
+ * DequantWeightMatrix (internal/ggml/gemm.go:240) decodes as Q5_K; so does
+ * this library.  F32 projection weights are multiplied as fp16 operands. */
 #define LE_TYPE_F32 0
 #define LE_TYPE_Q8_0 8
 #define LE_TYPE_Q4_K 12
@@ -82,6 +85,20 @@ int le_model_load(int dev, const le_tensor_desc* tensors, int n_tensors, const l
  * internal/gguf/reader.go:219-280) and call le_model_load. */
 int le_model_load_gguf(int dev, const char* path, le_model** out);
 
+/* Wall-clock phases of a model load and the replica's footprint (the
+ * reference's LoadBertModel + PreDequant, bert.go:91, bert.go:542, run once
+ * at Load).  Each phase is timed with the device idle before and after it. */
+typedef struct {
+  double parse_ms;      /* GGUF mmap + metadata parse (le_model_load_gguf) */
+  double upload_ms;     /* host -> device copies of the tensor bytes */
+  double repack_ms;     /* tile-blocked repack kernels */
+  double expand_ms;     /* fp16 operand matrices (expand or F32 convert) */
+  double total_ms;      /* the whole load call, parse included */
+  int64_t h2d_bytes;    /* weight and embedding bytes copied to the device */
+  int64_t weight_bytes; /* device memory held by the replica's weights */
+} le_load_stats;
+int le_model_load_stats(const le_model* m, le_load_stats* out);
+
 /* Release a model (bert.go:46 Close). */
 int le_model_free(le_model* m);
 
@@ -99,11 +116,21 @@ int le_model_hparams(const le_model* m, le_hparams* out);
 int le_embed_ids(le_model* const* models, int n_models, const int32_t* ids, const int32_t* seq_offsets, int nseq,
                  int out_dim, float* out);
 
+/* Largest n_tokens of one le_embed_ids_device call (le_embed_ids splits
+ * larger batches into calls of at most this many tokens). */
+#define LE_MAX_DEVICE_TOKENS 65536
+
 /* Same on device-resident buffers of the model's device, asynchronously on
  * `stream` (a cudaStream_t; NULL = the model's own stream).  d_offsets has
  * nseq+1 entries starting at 0; n_tokens = d_offsets[nseq]; max_len is the
  * longest sequence.  The call returns once the work is enqueued; device
- * errors surface from the next call or from le_sync. */
+ * errors surface from the next call or from le_sync.  All forwards of one
+ * model share its workspace: calls on different streams are ordered on the
+ * GPU (each waits for the previous call's completion event), so they run one
+ * after another, not concurrently.  A call enqueued while `stream` is being
+ * captured into the caller's CUDA graph is not ordered against other calls:
+ * the caller must not replay that graph concurrently with other forwards of
+ * the model. */
 int le_embed_ids_device(le_model* m, const int32_t* d_ids, const int32_t* d_offsets, int nseq, int n_tokens,
                         int max_len, int out_dim, float* d_out, void* stream);
 
@@ -128,6 +155,11 @@ int le_qgemm(int dev, int qtype, const void* wq, int N, int K, const float* x, i
 typedef struct le_qweight le_qweight;
 int le_qweight_create(int dev, int qtype, const void* wq, int N, int K, le_qweight** out);
 int le_qgemm_device(le_qweight* w, const float* d_x, int M, float* d_y, void* stream);
+/* Wait for the weight's device work (all streams of its device) and report a
+ * kernel failure of an earlier le_qgemm_device call (LE_EDEVICE; the status
+ * word is cleared).  le_qgemm_device returns once its work is enqueued, so
+ * this is where its device errors surface. */
+int le_qweight_sync(le_qweight* w);
 int le_qweight_free(le_qweight* w);
 
 /* le_qgemm_device without allocation (no counterpart in the reference: its Go

@@ -5,6 +5,7 @@
 #include <unistd.h>
 
 #include <algorithm>
+#include <chrono>
 #include <cmath>
 #include <cstdarg>
 #include <cstdio>
@@ -62,6 +63,10 @@ static long row_bytes_of(int type, long k) {
     default: return -1;
   }
 }
+
+// Projection weight types as DequantWeightMatrix reads them (gemm.go:224-263):
+// ids 15 and 16 share the Q5_K case there, so they decode as Q5_K here.
+static int weight_type(int type) { return (type == 15 || type == 16) ? T_Q5_K : type; }
 
 static bool is_quant(int type) { return type == T_Q8_0 || type == T_Q4_K || type == T_Q5_K || type == T_Q6_K; }
 
@@ -139,7 +144,16 @@ struct Workspace {
   HostBuf h_ids, h_offsets, h_out;
 };
 
-constexpr int CHUNK_TOKENS = 1 << 16;
+constexpr int CHUNK_TOKENS = LE_MAX_DEVICE_TOKENS;
+
+// Wall-clock phases of one model load (le_model_load_stats).
+struct LoadTimes {
+  double upload_ms = 0, repack_ms = 0, expand_ms = 0;
+  int64_t h2d_bytes = 0;
+};
+static double now_ms() {
+  return std::chrono::duration<double, std::milli>(std::chrono::steady_clock::now().time_since_epoch()).count();
+}
 
 }  // namespace
 
@@ -221,6 +235,11 @@ struct le_model {
   uint64_t graph_clock = 0;
   std::mutex mu;
   Workspace ws;
+  // Completion of the last forward enqueued on the workspace (any stream).
+  cudaEvent_t ws_done = nullptr;
+  bool ws_used = false;
+  LoadTimes load;
+  double parse_ms = 0, load_ms = 0;
   void drop_graphs() {
     for (auto& g : graphs)
       if (g.exec) cudaGraphExecDestroy(g.exec);
@@ -228,6 +247,7 @@ struct le_model {
   }
   ~le_model() {
     drop_graphs();
+    if (ws_done) cudaEventDestroy(ws_done);
     if (capture_stream) cudaStreamDestroy(capture_stream);
     if (stream) cudaStreamDestroy(stream);
   }
@@ -260,32 +280,61 @@ static int check_status(DevBuf& status, cudaStream_t s) {
 // ---------------------------------------------------------- weights -------
 
 // Upload raw GGUF rows of one or two source tensors and repack them into the
-// tile layout (interleave: merged ffn_up/ffn_gate).
+// tile layout (interleave: merged ffn_up/ffn_gate).  F32 weights (accepted
+// when allow_f32) keep their exact rows in `buf` and get only the fp16
+// operand matrix.
 static int make_qmat(QMat& q, int type, const void* src0, const void* src1, int N, int K, bool interleave,
-                     cudaStream_t s) {
-  if (!is_quant(type)) return fail(LE_EINVAL, "unsupported weight type %d (Q8_0/Q4_K/Q5_K/Q6_K only)", type);
+                     cudaStream_t s, bool allow_f32 = false, LoadTimes* lt = nullptr) {
+  LoadTimes scratch;
+  if (!lt) lt = &scratch;
+  const bool f32 = type == T_F32 && allow_f32;
+  if (!is_quant(type) && !f32)
+    return fail(LE_EINVAL, "unsupported weight type %d (F32/Q8_0/Q4_K/Q5_K/Q6_K only)", type);
   const long rb = row_bytes_of(type, K);
   if (rb < 0 || K % TILE_K) return fail(LE_EINVAL, "K=%d is not a multiple of the block size of type %d", K, type);
   if (N <= 0 || N % 2) return fail(LE_EINVAL, "N=%d must be positive and even", N);
   q.type = type;
-  q.qf = qfmt_of(type);
+  q.qf = f32 ? QF_F16 : qfmt_of(type);
   q.K = K;
   q.n_real = interleave ? 2 * N : N;
   int n_tiles = interleave ? (N + TILE_N / 2 - 1) / (TILE_N / 2) : (N + TILE_N - 1) / TILE_N;
   n_tiles += n_tiles & 1;  // even: the CTA-pair GEMM takes weight tiles two at a time
   q.n_virt = n_tiles * TILE_N;
   q.interleaved = interleave;
+  const size_t nb = (size_t)N * rb;
+  double t0 = now_ms();
+  lt->h2d_bytes += (int64_t)(nb * (interleave ? 2 : 1));
+  if (f32) {
+    TRY(q.buf.ensure(nb * (interleave ? 2 : 1)));
+    CK(cudaMemcpyAsync(q.buf.p, src0, nb, cudaMemcpyHostToDevice, s));
+    if (interleave) CK(cudaMemcpyAsync(q.buf.as<uint8_t>() + nb, src1, nb, cudaMemcpyHostToDevice, s));
+    CK(cudaStreamSynchronize(s));
+    lt->upload_ms += now_ms() - t0;
+    t0 = now_ms();
+    TRY(q.w16.ensure((size_t)q.n_virt * K * 2));
+    CK(launch_f32_rows_to_f16(q.buf.as<float>(), interleave ? q.buf.as<float>() + (size_t)N * K : nullptr, N, K,
+                              q.n_virt, interleave ? 1 : 0, q.w16.as<__half>(), s));
+    CK(cudaStreamSynchronize(s));
+    lt->expand_ms += now_ms() - t0;
+    return LE_OK;
+  }
   TRY(q.buf.ensure((size_t)n_tiles * (K / TILE_K) * chunk_bytes(q.qf)));
   DevBuf raw;
-  const size_t nb = (size_t)N * rb;
   TRY(raw.ensure(nb * (interleave ? 2 : 1)));
   CK(cudaMemcpyAsync(raw.p, src0, nb, cudaMemcpyHostToDevice, s));
   if (interleave) CK(cudaMemcpyAsync(raw.as<uint8_t>() + nb, src1, nb, cudaMemcpyHostToDevice, s));
+  CK(cudaStreamSynchronize(s));
+  lt->upload_ms += now_ms() - t0;
+  t0 = now_ms();
   CK(launch_repack(type, raw.as<uint8_t>(), interleave ? raw.as<uint8_t>() + nb : nullptr, rb, N, K, n_tiles,
                    interleave ? 1 : 0, q.buf.as<uint8_t>(), s));
+  CK(cudaStreamSynchronize(s));
+  lt->repack_ms += now_ms() - t0;
+  t0 = now_ms();
   TRY(q.w16.ensure((size_t)q.n_virt * K * 2));
   CK(launch_expand_f16(q.qf, q.buf.as<uint8_t>(), q.n_virt, K, q.w16.as<__half>(), s));
   CK(cudaStreamSynchronize(s));
+  lt->expand_ms += now_ms() - t0;
   return LE_OK;
 }
 
@@ -302,7 +351,11 @@ static int upload_f32(DevBuf& b, const le_tensor_desc* t, int n, cudaStream_t s)
 static int ensure_ws(le_model* m, int tokens, int seqs) {
   Workspace& w = m->ws;
   const int H = m->hp.hidden, F = m->hp.ffn;
-  if (tokens > w.cap_tokens || seqs > w.cap_seqs) m->drop_graphs();  // they point at the old buffers
+  if (tokens > w.cap_tokens || seqs > w.cap_seqs) {
+    m->drop_graphs();  // they point at the old buffers
+    // A forward still running on another stream may use the old buffers.
+    if (m->ws_used) CK(cudaEventSynchronize(m->ws_done));
+  }
   if (tokens > w.cap_tokens) {
     const size_t T = (size_t)std::max(tokens, 256);
     TRY(w.ids.ensure(T * 4));
@@ -345,6 +398,25 @@ static int model_status(le_model* m, cudaStream_t s) {
 }
 
 // ---------------------------------------------------------- forward -------
+
+// Every forward of a model uses its one workspace (activations, the fused
+// LayerNorm's statistics words), so forwards enqueued on different streams
+// must not overlap on the GPU: each waits for the completion event of the
+// previous one before its first kernel and records its own after its last.
+// Under stream capture (the caller's graph) the caller orders the replays.
+static int ws_order_begin(le_model* m, cudaStream_t s, bool* capturing) {
+  cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+  CK(cudaStreamIsCapturing(s, &cs));
+  *capturing = cs != cudaStreamCaptureStatusNone;
+  if (!*capturing && m->ws_used) CK(cudaStreamWaitEvent(s, m->ws_done, 0));
+  return LE_OK;
+}
+static int ws_order_end(le_model* m, cudaStream_t s, bool capturing) {
+  if (capturing) return LE_OK;
+  CK(cudaEventRecord(m->ws_done, s));
+  m->ws_used = true;
+  return LE_OK;
+}
 
 static int gemm(le_model* m, int cls, const QMat& W, const __half* A, int lda, const EpiParams& ep, cudaStream_t s) {
   m->prof.begin(cls, s);
@@ -409,7 +481,8 @@ static int forward(le_model* m, const int32_t* d_ids, const int32_t* d_offsets, 
       const QMat* q[4] = {&L.qkv, &L.out, &L.upgate, &L.down};
       const int modes[4] = {EPI_QKV, EPI_F32, EPI_GEGLU, EPI_F32};
       for (int i = 0; i < 4; i++)
-        sp.layers[l].g[i] = SmallGemm{q[i]->buf.as<uint8_t>(), q[i]->qf, q[i]->K, q[i]->n_virt / 2, modes[i]};
+        sp.layers[l].g[i] = SmallGemm{q[i]->qf == QF_F16 ? nullptr : q[i]->buf.as<uint8_t>(), q[i]->qf, q[i]->K,
+                                      q[i]->n_virt / 2, modes[i]};
       sp.layers[l].attn_w = L.attn_w.as<float>();
       sp.layers[l].attn_b = L.attn_b.as<float>();
       sp.layers[l].out_w = L.out_w.as<float>();
@@ -554,10 +627,13 @@ static int embed_host(le_model* m, const int32_t* ids, const int32_t* offs, int 
     int32_t* ho = w.h_offsets.as<int32_t>();
     std::memcpy(hi, ids + offs[s0], (size_t)T * 4);
     for (int i = 0; i <= n; i++) ho[i] = offs[s0 + i] - offs[s0];
+    bool cap = false;
+    TRY(ws_order_begin(m, s, &cap));
     CK(cudaMemcpyAsync(w.ids.p, hi, (size_t)T * 4, cudaMemcpyHostToDevice, s));
     CK(cudaMemcpyAsync(w.offsets.p, ho, (size_t)(n + 1) * 4, cudaMemcpyHostToDevice, s));
     TRY(run_forward(m, w.ids.as<int32_t>(), w.offsets.as<int32_t>(), n, T, maxlen, out_dim, w.out.as<float>(), s));
     CK(cudaMemcpyAsync(w.h_out.p, w.out.p, (size_t)n * out_dim * 4, cudaMemcpyDeviceToHost, s));
+    TRY(ws_order_end(m, s, cap));
     TRY(model_status(m, s));
     std::memcpy(out + (size_t)s0 * out_dim, w.h_out.p, (size_t)n * out_dim * 4);
     s0 = s1;
@@ -717,7 +793,9 @@ static const le_tensor_desc* find(const le_tensor_desc* t, int nt, const std::st
   return nullptr;
 }
 
-static int load_impl(int dev, const le_tensor_desc* ts, int nt, const le_hparams* hp, le_model** out) {
+static int load_impl(int dev, const le_tensor_desc* ts, int nt, const le_hparams* hp, le_model** out,
+                     double parse_ms = 0) {
+  const double t_start = now_ms();
   if (!ts || !hp || !out) return fail(LE_EINVAL, "null argument");
   *out = nullptr;
   int ndev = 0;
@@ -738,6 +816,7 @@ static int load_impl(int dev, const le_tensor_desc* ts, int nt, const le_hparams
   m->head_dim = hp->hidden / hp->heads;
   CK(cudaStreamCreateWithFlags(&m->stream, cudaStreamNonBlocking));
   CK(cudaStreamCreateWithFlags(&m->capture_stream, cudaStreamNonBlocking));
+  CK(cudaEventCreateWithFlags(&m->ws_done, cudaEventDisableTiming));
   CK(cudaDeviceGetAttribute(&m->sms, cudaDevAttrMultiProcessorCount, dev));
   TRY(m->barrier.ensure(16));
   cudaStream_t s = m->stream;
@@ -755,7 +834,13 @@ static int load_impl(int dev, const le_tensor_desc* ts, int nt, const le_hparams
   m->vocab = te->n_dims > 1 ? (int)te->dims[1] : 1;
   if (te->n_bytes < m->emb_row_bytes * m->vocab) return fail(LE_EINVAL, "token_embd.weight too short");
   TRY(m->emb.ensure((size_t)m->emb_row_bytes * m->vocab));
-  CK(cudaMemcpyAsync(m->emb.p, te->data, (size_t)m->emb_row_bytes * m->vocab, cudaMemcpyHostToDevice, s));
+  {
+    const double t0 = now_ms();
+    CK(cudaMemcpyAsync(m->emb.p, te->data, (size_t)m->emb_row_bytes * m->vocab, cudaMemcpyHostToDevice, s));
+    CK(cudaStreamSynchronize(s));
+    m->load.upload_ms += now_ms() - t0;
+    m->load.h2d_bytes += (int64_t)m->emb_row_bytes * m->vocab;
+  }
   // token_types row 0, exact float32 (bert.go:227), kept in its own buffer.
   {
     const long trb = row_bytes_of(tt->type, H);
@@ -788,15 +873,20 @@ static int load_impl(int dev, const le_tensor_desc* ts, int nt, const le_hparams
       if (w[j]->dims[0] != Ks[j] || N != Ns[j])
         return fail(LE_EINVAL, "%s%s.weight has shape [%lld, %lld], expected [%d, %d]", p.c_str(), names[j],
                     (long long)w[j]->dims[0], (long long)N, Ks[j], Ns[j]);
-      if (w[j]->n_bytes < row_bytes_of(w[j]->type, Ks[j]) * Ns[j])
+      if (row_bytes_of(weight_type(w[j]->type), Ks[j]) < 0)
+        return fail(LE_EINVAL, "%s%s.weight: unsupported type %d (F32/Q8_0/Q4_K/Q5_K/Q6_K)", p.c_str(), names[j],
+                    w[j]->type);
+      if (w[j]->n_bytes < row_bytes_of(weight_type(w[j]->type), Ks[j]) * Ns[j])
         return fail(LE_EINVAL, "%s%s.weight data too short", p.c_str(), names[j]);
     }
-    if (w[2]->type != w[3]->type)
+    int ty[5];
+    for (int j = 0; j < 5; j++) ty[j] = weight_type(w[j]->type);
+    if (ty[2] != ty[3])
       return fail(LE_EINVAL, "ffn_up and ffn_gate of layer %d must share a type (%d vs %d)", i, w[2]->type, w[3]->type);
-    TRY(make_qmat(L.qkv, w[0]->type, w[0]->data, nullptr, 3 * H, H, false, s));
-    TRY(make_qmat(L.out, w[1]->type, w[1]->data, nullptr, H, H, false, s));
-    TRY(make_qmat(L.upgate, w[2]->type, w[2]->data, w[3]->data, F, H, true, s));
-    TRY(make_qmat(L.down, w[4]->type, w[4]->data, nullptr, H, F, false, s));
+    TRY(make_qmat(L.qkv, ty[0], w[0]->data, nullptr, 3 * H, H, false, s, true, &m->load));
+    TRY(make_qmat(L.out, ty[1], w[1]->data, nullptr, H, H, false, s, true, &m->load));
+    TRY(make_qmat(L.upgate, ty[2], w[2]->data, w[3]->data, F, H, true, s, true, &m->load));
+    TRY(make_qmat(L.down, ty[4], w[4]->data, nullptr, H, F, false, s, true, &m->load));
     const char* nn[4] = {"attn_output_norm.weight", "attn_output_norm.bias", "layer_output_norm.weight",
                          "layer_output_norm.bias"};
     DevBuf* dst[4] = {&L.attn_w, &L.attn_b, &L.out_w, &L.out_b};
@@ -826,6 +916,8 @@ static int load_impl(int dev, const le_tensor_desc* ts, int nt, const le_hparams
   TRY(m->status.ensure(sizeof(DevStatus)));
   CK(cudaMemsetAsync(m->status.p, 0, sizeof(DevStatus), s));
   CK(cudaStreamSynchronize(s));
+  m->parse_ms = parse_ms;
+  m->load_ms = parse_ms + (now_ms() - t_start);
   *out = m.release();
   return LE_OK;
 }
@@ -836,6 +928,7 @@ int le_model_load(int dev, const le_tensor_desc* tensors, int n_tensors, const l
 
 int le_model_load_gguf(int dev, const char* path, le_model** out) {
   if (!path || !out) return fail(LE_EINVAL, "null argument");
+  const double t0 = now_ms();
   Mapped mp;
   const int fd = open(path, O_RDONLY);
   if (fd < 0) return fail(LE_EIO, "gguf: open %s: %s", path, strerror(errno));
@@ -860,7 +953,7 @@ int le_model_load_gguf(int dev, const char* path, le_model** out) {
   hp.context_length = (int)u("nomic-bert.context_length");
   hp.ln_eps = f("nomic-bert.attention.layer_norm_epsilon");
   hp.rope_base = f("nomic-bert.rope.freq_base");
-  return load_impl(dev, g.tensors.data(), (int)g.tensors.size(), &hp, out);
+  return load_impl(dev, g.tensors.data(), (int)g.tensors.size(), &hp, out, now_ms() - t0);
 }
 
 int le_model_free(le_model* m) {
@@ -871,6 +964,23 @@ int le_model_free(le_model* m) {
     cudaStreamSynchronize(m->stream);
   }
   delete m;
+  return LE_OK;
+}
+
+int le_model_load_stats(const le_model* m, le_load_stats* out) {
+  if (!m || !out) return fail(LE_EINVAL, "null argument");
+  out->parse_ms = m->parse_ms;
+  out->upload_ms = m->load.upload_ms;
+  out->repack_ms = m->load.repack_ms;
+  out->expand_ms = m->load.expand_ms;
+  out->total_ms = m->load_ms;
+  out->h2d_bytes = m->load.h2d_bytes;
+  size_t dev_bytes = m->emb.n + m->type0.n + m->embd_w.n + m->embd_b.n + m->rope_cos.n + m->rope_sin.n;
+  for (const Layer& L : m->layers) {
+    for (const QMat* q : {&L.qkv, &L.out, &L.upgate, &L.down}) dev_bytes += q->buf.n + q->w16.n;
+    dev_bytes += L.attn_w.n + L.attn_b.n + L.out_w.n + L.out_b.n;
+  }
+  out->weight_bytes = (int64_t)dev_bytes;
   return LE_OK;
 }
 
@@ -936,11 +1046,17 @@ int le_embed_ids_device(le_model* m, const int32_t* d_ids, const int32_t* d_offs
   if (out_dim < 1 || out_dim > m->hp.hidden) return fail(LE_EINVAL, "out_dim %d outside [1, %d]", out_dim, m->hp.hidden);
   if (nseq < 0 || n_tokens < 0 || max_len < 0 || max_len > m->hp.context_length)
     return fail(LE_EINVAL, "bad sizes (nseq %d, tokens %d, max_len %d)", nseq, n_tokens, max_len);
+  if (n_tokens > LE_MAX_DEVICE_TOKENS)
+    return fail(LE_EINVAL, "n_tokens %d exceeds LE_MAX_DEVICE_TOKENS (%d): split the batch", n_tokens,
+                LE_MAX_DEVICE_TOKENS);
   std::lock_guard<std::mutex> lk(m->mu);
   CK(cudaSetDevice(m->dev));
   cudaStream_t s = stream ? (cudaStream_t)stream : m->stream;
   TRY(ensure_ws(m, n_tokens, nseq));
-  return run_forward(m, d_ids, d_offsets, nseq, n_tokens, max_len, out_dim, d_out, s);
+  bool cap = false;
+  TRY(ws_order_begin(m, s, &cap));
+  TRY(run_forward(m, d_ids, d_offsets, nseq, n_tokens, max_len, out_dim, d_out, s));
+  return ws_order_end(m, s, cap);
 }
 
 int le_sync(le_model* m) {
@@ -987,22 +1103,36 @@ int le_dequant(le_model* m, int layer, int which, int mode, float* out) {
   CK(cudaSetDevice(m->dev));
   const Layer& L = m->layers[layer];
   const QMat* q = which == 0 ? &L.qkv : which == 1 ? &L.out : which == 4 ? &L.down : &L.upgate;
+  const int K = q->K;
+  // Virtual row of output row n (the merged up/gate order for which 2, 3).
+  auto vrow = [&](int n) {
+    return (which == 2 || which == 3) ? (n / (TILE_N / 2)) * TILE_N + (n % (TILE_N / 2)) + (which == 3 ? TILE_N / 2 : 0)
+                                      : n;
+  };
+  const int n_out = (which == 2 || which == 3) ? m->hp.ffn : q->n_real;
+  if (q->qf == QF_F16) {
+    // F32 weights: mode 0 is the stored rows themselves, mode 1 their fp16
+    // operand values.
+    if (mode == 0) {
+      const size_t off = which == 3 ? (size_t)n_out * K : 0;
+      CK(cudaMemcpyAsync(out, q->buf.as<float>() + off, (size_t)n_out * K * 4, cudaMemcpyDeviceToHost, m->stream));
+      CK(cudaStreamSynchronize(m->stream));
+      return LE_OK;
+    }
+    std::vector<__half> h16((size_t)q->n_virt * K);
+    CK(cudaMemcpyAsync(h16.data(), q->w16.p, h16.size() * 2, cudaMemcpyDeviceToHost, m->stream));
+    CK(cudaStreamSynchronize(m->stream));
+    for (int n = 0; n < n_out; n++)
+      for (int k = 0; k < K; k++) out[(size_t)n * K + k] = __half2float(h16[(size_t)vrow(n) * K + k]);
+    return LE_OK;
+  }
   DevBuf d;
   TRY(d.ensure((size_t)q->n_virt * q->K * 4));
   CK(launch_dequant_tiles(q->qf, q->buf.as<uint8_t>(), q->n_virt, q->K, mode, d.as<float>(), m->stream));
   std::vector<float> all((size_t)q->n_virt * q->K);
   CK(cudaMemcpyAsync(all.data(), d.p, all.size() * 4, cudaMemcpyDeviceToHost, m->stream));
   CK(cudaStreamSynchronize(m->stream));
-  const int K = q->K;
-  if (which == 2 || which == 3) {
-    const int F = m->hp.ffn;
-    for (int n = 0; n < F; n++) {
-      const int v = (n / (TILE_N / 2)) * TILE_N + (n % (TILE_N / 2)) + (which == 3 ? TILE_N / 2 : 0);
-      std::memcpy(out + (size_t)n * K, all.data() + (size_t)v * K, (size_t)K * 4);
-    }
-  } else {
-    std::memcpy(out, all.data(), (size_t)q->n_real * K * 4);
-  }
+  for (int n = 0; n < n_out; n++) std::memcpy(out + (size_t)n * K, all.data() + (size_t)vrow(n) * K, (size_t)K * 4);
   return LE_OK;
 }
 
@@ -1040,6 +1170,14 @@ int le_qgemm_device(le_qweight* w, const float* d_x, int M, float* d_y, void* st
   CK(launch_gemm(w->w.qf, w->w.buf.as<uint8_t>(), w->w.w16.as<__half>(), w->w.n_real, K, w->x16.as<__half>(), K, e,
                  w->status.as<DevStatus>(), s));
   return LE_OK;
+}
+
+int le_qweight_sync(le_qweight* w) {
+  if (!w) return fail(LE_EINVAL, "null argument");
+  std::lock_guard<std::mutex> lk(w->mu);
+  CK(cudaSetDevice(w->dev));
+  CK(cudaDeviceSynchronize());
+  return check_status(w->status, w->stream);
 }
 
 int le_qweight_free(le_qweight* w) {

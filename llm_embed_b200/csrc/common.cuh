@@ -61,6 +61,10 @@ constexpr int TILE_K = 64;
 constexpr int TILE_Q_BYTES = TILE_N * TILE_K;  // 8192
 
 enum QFmt : int { QF_Q8_0 = 0, QF_KMIN = 1, QF_Q6K = 2 };
+// F32 GGUF weights have no tile-blocked copy: they are held only as the fp16
+// operand matrix (and their exact float32 rows for le_dequant), and every
+// GEMM on them runs the fp16-operand tensor-core kernel.
+constexpr int QF_F16 = 3;
 
 __host__ __device__ constexpr int qfmt_of(int ggml_type) {
   return ggml_type == T_Q8_0 ? QF_Q8_0 : (ggml_type == T_Q6_K ? QF_Q6K : QF_KMIN);

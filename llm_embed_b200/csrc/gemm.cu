@@ -8,6 +8,11 @@ cudaError_t launch_gemm(int qf, const uint8_t* W, const __half* W16, int n_virtu
                         const EpiParams& ep, DevStatus* status, cudaStream_t s) {
   // The tensor-core kernels write through TMA: output rows 16-byte aligned.
   const bool tma_ok = ep.mode == EPI_F32 ? ep.ldo % 4 == 0 : ep.ldo % 8 == 0;
+  // F32 weights exist only as fp16 operands: the TMA kernel at every M.
+  if (qf == QF_F16) {
+    if (!W16 || n_virtual % (2 * TILE_N) || !tma_ok) return cudaErrorInvalidValue;
+    return launch_gemm_f16(W16, n_virtual, K, A, lda, ep, status, s);
+  }
   if (ep.M >= TC_MIN_M && n_virtual % (2 * TILE_N) == 0 && tma_ok) {
     if (ep.M >= TC_F16_MIN_M && W16) return launch_gemm_f16(W16, n_virtual, K, A, lda, ep, status, s);
     return launch_gemm_tc2(qf, W, n_virtual, K, A, lda, ep, status, s);

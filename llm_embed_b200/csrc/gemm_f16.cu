@@ -97,9 +97,6 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NTHREADS, 1)
   const int ksteps = K / BK;
   const int total = m_tiles * n_tiles;
   const int cluster = blockIdx.x >> 1, nclusters = gridDim.x >> 1;
-#ifdef LE_TC_WAITPROF
-  const long long t_kernel0 = clock64();
-#endif
 
   if (threadIdx.x == 0) {
     *abort_flag = 0;
@@ -215,9 +212,6 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NTHREADS, 1)
     tc_fence_after();
     asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(TMEM_COLS));
   }
-#ifdef LE_TC_WAITPROF
-  if (threadIdx.x == 0) atomicAdd(&g_waitprof[0], (unsigned long long)(clock64() - t_kernel0));
-#endif
 }
 
 // ---------------------------------------------------------------- host ----
@@ -312,16 +306,6 @@ static cudaError_t launch(const __half* W16, int n_virtual, int K, const __half*
 
 }  // namespace tcf
 
-#ifdef LE_TC_WAITPROF
-extern "C" int le_debug_waitprof3(unsigned long long* out, int reset) {
-  if (cudaMemcpyFromSymbol(out, tcx::g_waitprof, sizeof(tcx::g_waitprof)) != cudaSuccess) return -2;
-  if (reset) {
-    unsigned long long z[10] = {};
-    if (cudaMemcpyToSymbol(tcx::g_waitprof, z, sizeof(z)) != cudaSuccess) return -2;
-  }
-  return 0;
-}
-#endif
 
 cudaError_t launch_gemm_f16(const __half* W16, int n_virtual, int K, const __half* A, long lda, const EpiParams& ep,
                             DevStatus* status, cudaStream_t s) {

@@ -171,9 +171,6 @@ __global__ void __launch_bounds__(NTHREADS, 1)
   const int ksteps = K / BK;
   const int total = m_tiles * NT;
   const int pair = blockIdx.x >> 1, npairs = gridDim.x >> 1;
-#ifdef LE_TC_WAITPROF
-  const long long t_kernel0 = clock64();
-#endif
 
   if (threadIdx.x == 0) {
     *abort_flag = 0;
@@ -305,9 +302,6 @@ __global__ void __launch_bounds__(NTHREADS, 1)
       ok = __all_sync(0xffffffffu, mbar_wait(tfull(acc), (tcount >> 1) & 1, abort_flag, status, 74));
       if (!ok) break;
       tc_fence_after();
-#ifdef LE_TC_WAITPROF
-      long long tp = clock64();
-#endif
       // Pass 1.  Chunk column 4l + i belongs to lane l of ln_row_stats;
       // q*[l] are those lanes' values.
       float qs[32], qss[32];
@@ -348,10 +342,6 @@ __global__ void __launch_bounds__(NTHREADS, 1)
           qs[l] = __fadd_rn(qs[l], qs[l + o]);
           qss[l] = __fadd_rn(qss[l], qss[l + o]);
         }
-#ifdef LE_TC_WAITPROF
-      if (lane == 0) atomicAdd(&g_waitprof[7], (unsigned long long)(clock64() - tp));
-      tp = clock64();
-#endif
       // Exchange the chunk totals: this lane's row, all six chunks.
       const long row = row0 + lane;
       st_relaxed_u64(cur + row * NCHUNK + chunk,
@@ -394,10 +384,6 @@ __global__ void __launch_bounds__(NTHREADS, 1)
       float mean, inv;
       ln_stats(ts, tss, HID, eps, &mean, &inv);
       asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
-#ifdef LE_TC_WAITPROF
-      if (lane == 0) atomicAdd(&g_waitprof[8], (unsigned long long)(clock64() - tp));
-      tp = clock64();
-#endif
       // Pass 2: 64 columns at a time -> two float32 blocks, one fp16 block.
       // A block wholly past the last token is not stored.
 #pragma unroll 1
@@ -426,9 +412,6 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         emit<NSTG>(&tmap_h, stage, obuf, reinterpret_cast<const uint32_t*>(b), col + c + 32, row0);
         emit<NSTG>(&tmap_o, stage, obuf, w16, col + c, row0);
       }
-#ifdef LE_TC_WAITPROF
-      if (lane == 0) atomicAdd(&g_waitprof[9], (unsigned long long)(clock64() - tp));
-#endif
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive_cluster(tempty_leader0 + 8 * acc);
@@ -456,9 +439,6 @@ __global__ void __launch_bounds__(NTHREADS, 1)
       ctl[1] = epoch + 1;
     }
   }
-#ifdef LE_TC_WAITPROF
-  if (threadIdx.x == 0) atomicAdd(&g_waitprof[0], (unsigned long long)(clock64() - t_kernel0));
-#endif
 }
 
 static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
@@ -487,9 +467,6 @@ static bool encode_2d(PFN_cuTensorMapEncodeTiled_v12000 enc, CUtensorMap* map, C
              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-#ifdef LE_TC_WAITPROF
-static int g_ln_pairs = 0;
-#endif
 
 }  // namespace tcl
 
@@ -546,24 +523,22 @@ static cudaError_t launch_layout(const CUtensorMap& amap, const CUtensorMap& bma
   const int m_tiles = (M + PM - 1) / PM;
   const int total = m_tiles * NT;
   const int pairs = total < npairs ? total : npairs;
-#ifdef LE_TC_WAITPROF
-  g_ln_pairs = pairs;
-#endif
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(2 * pairs);
   cfg.blockDim = dim3(NTHREADS);
   cfg.dynamicSmemBytes = L::ALLOC;
   cfg.stream = s;
   cfg.attrs = attr;
-  // LLMEMBED_LN_NONCOOPERATIVE=1 drops the cooperative attribute, for
-  // profilers that cannot replay cooperative cluster launches (Nsight
-  // Compute); the grid still fits the GPU, so on an otherwise idle GPU all
-  // pairs are resident all the same.
-  static const bool noncoop = [] {
-    const char* v = std::getenv("LLMEMBED_LN_NONCOOPERATIVE");
-    return v && v[0] == '1';
-  }();
-  cfg.numAttrs = noncoop ? 1 : 2;
+#ifdef LE_LN_NONCOOPERATIVE
+  // Profiling builds only (nvcc -DLE_LN_NONCOOPERATIVE): Nsight Compute
+  // cannot replay cooperative cluster launches, so this build launches
+  // without the cooperative attribute.  The grid still fits an otherwise
+  // idle GPU, but co-residency of the CTAs (which wait on each other's
+  // statistics) is then not guaranteed; release builds never take it.
+  cfg.numAttrs = 1;
+#else
+  cfg.numAttrs = 2;
+#endif
   return cudaLaunchKernelEx(&cfg, gemm_ln_kernel<L>, amap, bmap, hmap, omap, K, M, m_tiles, h, ln_w, ln_b, eps, part,
                             part_rows, ctl, status);
 }
@@ -593,37 +568,5 @@ cudaError_t launch_gemm_ln(const __half* W16, int K, const __half* A, long lda, 
   return launch_layout<LayLongK>(amap, bmap, hmap, omap, K, M, h, ln_w, ln_b, eps, part, part_rows, ctl, status, s);
 }
 
-#ifdef LE_TC_WAITPROF
-// Profiling build only: wait counters of this file's kernel and a direct
-// launch with buffers of its own.
-extern "C" int le_debug_waitprof_ln(unsigned long long* out, int reset) {
-  if (cudaMemcpyFromSymbol(out, tcx::g_waitprof, sizeof(tcx::g_waitprof)) != cudaSuccess) return -2;
-  if (reset) {
-    unsigned long long z[10] = {};
-    if (cudaMemcpyToSymbol(tcx::g_waitprof, z, sizeof(z)) != cudaSuccess) return -2;
-  }
-  return 0;
-}
-extern "C" int le_debug_gemm_ln(const void* W16, int K, const void* A, long lda, int M, float* h, void* out16,
-                                const float* lw, const float* lb, float eps, void* stream) {
-  static DevStatus* st = nullptr;
-  static void* part = nullptr;
-  static void* ctl = nullptr;
-  static int rows = 0;
-  if (!st && (cudaMalloc(&st, sizeof(DevStatus)) != cudaSuccess || cudaMalloc(&ctl, 16) != cudaSuccess)) return -2;
-  if (gemm_ln_part_rows(M) > rows) {
-    cudaFree(part);
-    rows = gemm_ln_part_rows(M);
-    if (cudaMalloc(&part, gemm_ln_part_bytes(M)) != cudaSuccess) return -2;
-    cudaMemset(part, 0xFF, gemm_ln_part_bytes(M));
-    cudaMemset(ctl, 0, 16);
-  }
-  const cudaError_t e = launch_gemm_ln(static_cast<const __half*>(W16), K, static_cast<const __half*>(A), lda, M, h,
-                                       static_cast<__half*>(out16), lw, lb, eps,
-                                       static_cast<unsigned long long*>(part), rows, static_cast<unsigned*>(ctl), st,
-                                       static_cast<cudaStream_t>(stream));
-  return e == cudaSuccess ? tcl::g_ln_pairs : -(int)e;
-}
-#endif
 
 }  // namespace le

@@ -15,6 +15,8 @@ cudaError_t launch_repack(int type, const uint8_t* src0, const uint8_t* src1, lo
 cudaError_t launch_dequant_tiles(int qf, const uint8_t* w, int n_rows, int K, int mode, float* out, cudaStream_t s);
 cudaError_t launch_gguf_rows(int type, const uint8_t* src, long row_bytes, int n_rows, int K, float* out, cudaStream_t s);
 cudaError_t launch_expand_f16(int qf, const uint8_t* w, int n_rows, int K, __half* out, cudaStream_t s);
+cudaError_t launch_f32_rows_to_f16(const float* src0, const float* src1, int N_src, int K, int n_virt, int interleave,
+                                   __half* out, cudaStream_t s);
 
 // elementwise.cu
 cudaError_t launch_embed_ln(const int32_t* ids, int emb_type, const uint8_t* emb, long emb_row_bytes, int vocab,

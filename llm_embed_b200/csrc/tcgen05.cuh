@@ -73,12 +73,6 @@ __device__ __forceinline__ bool mbar_wait_sleep(uint32_t bar, uint32_t parity, v
   }
 }
 
-#ifdef LE_TC_WAITPROF
-// Profiling build only: clock cycles each role spends in mbarrier waits, by
-// wait site (1 producer/empty_ld, 2 MMA/tempty, 3 MMA/full_ld, 4 MMA/full_b,
-// 5 dequant/full_ld, 6 dequant/empty_b, 7 epilogue/tfull), 0 = kernel cycles.
-static __device__ unsigned long long g_waitprof[10];
-#endif
 
 // Bounded wait: false (and the abort flag set, DE_TIMEOUT recorded) if the
 // phase does not complete within WAIT_LIMIT_NS or another role aborted.
@@ -88,15 +82,7 @@ __device__ __forceinline__ bool mbar_wait_impl(uint32_t bar, uint32_t parity, vo
 template <bool CLUSTER = false>
 __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile int* abort_flag, DevStatus* st,
                                           int site) {
-#ifdef LE_TC_WAITPROF
-  const long long t0 = clock64();
-  const bool ok = mbar_wait_impl<CLUSTER>(bar, parity, abort_flag, st, site);
-  const int ps = site % 10;  // recorded by lane 0 of every waiting warp
-  if ((threadIdx.x & 31) == 0) atomicAdd(&g_waitprof[ps], (unsigned long long)(clock64() - t0));
-  return ok;
-#else
   return mbar_wait_impl<CLUSTER>(bar, parity, abort_flag, st, site);
-#endif
 }
 template <bool CLUSTER>
 __device__ __forceinline__ bool mbar_wait_impl(uint32_t bar, uint32_t parity, volatile int* abort_flag, DevStatus* st,

@@ -123,6 +123,32 @@ __global__ void expand_f16_kernel(const uint8_t* __restrict__ w, int n_rows, int
   *reinterpret_cast<uint4*>(out + (long)v * K + ks * TILE_K + g * 8) = dq8_f16<QF>(u, chunk + TILE_Q_BYTES, r, g);
 }
 
+// F32 weight rows (DequantWeightMatrix case 0, gemm.go:257-263: the values
+// themselves) to the fp16 operand matrix [n_virt][K] in virtual row order
+// (the merged up/gate order of repack_kernel when interleave), rows past the
+// source zero.  One thread per 8 consecutive elements.
+__global__ void f32_rows_to_f16_kernel(const float* __restrict__ src0, const float* __restrict__ src1, int N_src, int K,
+                                       int n_virt, int interleave, __half* __restrict__ out) {
+  const long idx = (long)blockIdx.x * blockDim.x + threadIdx.x;
+  const int groups = K / 8;
+  if (idx >= (long)n_virt * groups) return;
+  const int v = (int)(idx / groups), c = (int)(idx % groups) * 8;
+  const float* row = nullptr;
+  if (interleave) {
+    const int t = v / TILE_N, r = v % TILE_N, srow = t * (TILE_N / 2) + (r % (TILE_N / 2));
+    if (srow < N_src) row = (r < TILE_N / 2 ? src0 : src1) + (long)srow * K;
+  } else if (v < N_src) {
+    row = src0 + (long)v * K;
+  }
+  uint4 h = make_uint4(0, 0, 0, 0);
+  if (row) {
+    const float4 a = *reinterpret_cast<const float4*>(row + c);
+    const float4 b = *reinterpret_cast<const float4*>(row + c + 4);
+    h = make_uint4(pack_half2(a.x, a.y), pack_half2(a.z, a.w), pack_half2(b.x, b.y), pack_half2(b.z, b.w));
+  }
+  *reinterpret_cast<uint4*>(out + (long)v * K + c) = h;
+}
+
 // Dequantise whole GGUF rows (used for the embedding table check).
 __global__ void gguf_rows_kernel(int type, const uint8_t* __restrict__ src, long row_bytes, int n_rows, int K,
                                  float* __restrict__ out) {
@@ -164,6 +190,14 @@ cudaError_t launch_dequant_tiles(int qf, const uint8_t* w, int n_rows, int K, in
 cudaError_t launch_gguf_rows(int type, const uint8_t* src, long row_bytes, int n_rows, int K, float* out, cudaStream_t s) {
   const long n = (long)n_rows * K;
   gguf_rows_kernel<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(type, src, row_bytes, n_rows, K, out);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_f32_rows_to_f16(const float* src0, const float* src1, int N_src, int K, int n_virt, int interleave,
+                                   __half* out, cudaStream_t s) {
+  if (K % 8) return cudaErrorInvalidValue;
+  const long n = (long)n_virt * (K / 8);
+  f32_rows_to_f16_kernel<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(src0, src1, N_src, K, n_virt, interleave, out);
   return cudaGetLastError();
 }
 

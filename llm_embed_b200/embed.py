@@ -46,6 +46,16 @@ class Stats(C.Structure):
     _fields_ = [("launches", C.c_int64), ("count", C.c_int64 * NCLASS), ("ms", C.c_double * NCLASS)]
 
 
+class LoadStats(C.Structure):
+    _fields_ = [("parse_ms", C.c_double), ("upload_ms", C.c_double), ("repack_ms", C.c_double),
+                ("expand_ms", C.c_double), ("total_ms", C.c_double), ("h2d_bytes", C.c_int64),
+                ("weight_bytes", C.c_int64)]
+
+
+# Largest token count of one device call (LE_MAX_DEVICE_TOKENS).
+MAX_DEVICE_TOKENS = 65536
+
+
 class HParams(C.Structure):
     _fields_ = [("n_layers", C.c_int32), ("hidden", C.c_int32), ("ffn", C.c_int32), ("heads", C.c_int32),
                 ("context_length", C.c_int32), ("ln_eps", C.c_float), ("rope_base", C.c_float)]
@@ -70,6 +80,7 @@ def lib() -> C.CDLL:
             L.le_model_load_gguf.argtypes = [C.c_int, C.c_char_p, C.POINTER(vp)]
             L.le_model_free.argtypes = [vp]
             L.le_model_hparams.argtypes = [vp, C.POINTER(HParams)]
+            L.le_model_load_stats.argtypes = [vp, C.POINTER(LoadStats)]
             L.le_embed_ids.argtypes = [C.POINTER(vp), C.c_int, ip, ip, C.c_int, C.c_int, fp]
             L.le_embed_ids_device.argtypes = [vp, vp, vp, C.c_int, C.c_int, C.c_int, C.c_int, vp, vp]
             L.le_sync.argtypes = [vp]
@@ -79,6 +90,7 @@ def lib() -> C.CDLL:
             L.le_qgemm_device.argtypes = [vp, vp, C.c_int, vp, vp]
             L.le_qgemm_device_noalloc.argtypes = [vp, vp, C.c_int, vp, vp]
             L.le_qweight_free.argtypes = [vp]
+            L.le_qweight_sync.argtypes = [vp]
             L.le_info.argtypes = [C.c_char_p, C.c_int]
             L.le_set_profiling.argtypes = [vp, C.c_int]
             L.le_get_stats.argtypes = [vp, C.POINTER(Stats), C.c_int]
@@ -246,6 +258,12 @@ class Embedder:
     def sync(self, replica: int = 0) -> None:
         _check(lib().le_sync(self._handles[replica]))
 
+    def load_stats(self, replica: int = 0) -> dict:
+        """Wall-clock phases (ms) of the replica's load and its byte counts."""
+        st = LoadStats()
+        _check(lib().le_model_load_stats(self._handles[replica], C.byref(st)))
+        return {f: getattr(st, f) for f, _ in LoadStats._fields_}
+
     def set_profiling(self, on: bool, replica: int = 0) -> None:
         _check(lib().le_set_profiling(self._handles[replica], 1 if on else 0))
 
@@ -286,6 +304,11 @@ class QWeight:
 
     def matmul_device(self, d_x: int, M: int, d_y: int, stream: int = 0) -> None:
         _check(lib().le_qgemm_device(self._h, d_x, M, d_y, stream or None))
+
+    def sync(self) -> None:
+        """Wait for the device work; raise on a kernel failure of an earlier
+        matmul_device call."""
+        _check(lib().le_qweight_sync(self._h))
 
     # Largest M*K le_qgemm_device_noalloc accepts (LE_QGEMM_NOALLOC_MAX_ELEMS).
     NOALLOC_MAX_ELEMS = 4 * 1024 * 1024

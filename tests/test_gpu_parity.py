@@ -5,6 +5,7 @@ Tolerances:
   * every embedding: cosine >= 0.99999 and max |diff| <= 2e-3 against the
     oracle's restatement of the reference's Go forward pass.
 """
+import json
 import os
 import threading
 
@@ -23,7 +24,16 @@ MAX_ABS = 2e-3
 NTHREADS = os.cpu_count() or 8
 
 
-def assert_parity(got, ref, cos_min=COS_MIN, max_abs=MAX_ABS):
+def log_parity(tag, **fields):
+    """Append one JSON record to $LLMEMBED_PARITY_LOG (if set): the parity
+    figures behind the committed per-config table."""
+    path = os.environ.get("LLMEMBED_PARITY_LOG")
+    if path:
+        with open(path, "a") as f:
+            f.write(json.dumps({"case": tag, **fields}) + "\n")
+
+
+def assert_parity(got, ref, cos_min=COS_MIN, max_abs=MAX_ABS, tag=None):
     got = np.asarray(got, np.float32)
     ref = np.asarray(ref, np.float32)
     assert got.shape == ref.shape
@@ -31,6 +41,8 @@ def assert_parity(got, ref, cos_min=COS_MIN, max_abs=MAX_ABS):
     nz = np.linalg.norm(ref, axis=1) > 0
     cos = (got * ref).sum(1)[nz] / (np.linalg.norm(got, axis=1)[nz] * np.linalg.norm(ref, axis=1)[nz])
     err = np.abs(got - ref).max() if got.size else 0.0
+    if tag:
+        log_parity(tag, n=int(got.shape[0]), min_cos=float(cos.min()) if cos.size else 1.0, max_abs=float(err))
     assert (cos.min() if cos.size else 1.0) >= cos_min, f"min cosine {cos.min():.8f}"
     assert err <= max_abs, f"max abs diff {err:.3e}"
     return cos, err
@@ -101,12 +113,17 @@ def test_config0_single_embed(model_path):
     finally:
         e.Close()
     ref = _oracle_embed(path, ids, offs)
-    assert_parity(got[None], ref)
+    assert_parity(got[None], ref, tag="configs[0] q8_0, batch 1, 8 tokens")
 
 
-@pytest.mark.parametrize("name,config,nseq", [("q8_0", 2, 24), ("q4_k_m", 3, 6), ("q6_k", 4, 2), ("q5_k", 4, 2)])
+@pytest.mark.parametrize("name,config,nseq", [("q8_0", 2, 256), ("q4_k_m", 3, 64), ("q6_k", 4, 16), ("q5_k", 4, 16)])
 def test_config_parity(model_path, name, config, nseq):
-    """First `nseq` sequences of configs[2..4] on their 12-layer models."""
+    """configs[2..4] on their 12-layer models against the oracle: the whole
+    configs[2] batch (256 sequences, the tcgen05 GEMMs with the fused
+    LayerNorm and the short-sequence attention), 64 configs[3] sequences
+    (Q4_K/Q6_K, lengths 64..256: both attention kernels) and 16 configs[4]
+    sequences of 512 tokens per Q6_K and Q5_K (8,192 tokens: fused
+    LayerNorm, long-sequence attention)."""
     path = model_path(name)
     ids, offs = synth.config_inputs(config)
     offs = offs[:nseq + 1]
@@ -117,7 +134,7 @@ def test_config_parity(model_path, name, config, nseq):
     finally:
         e.Close()
     ref = _oracle_embed(path, ids, offs)
-    assert_parity(got, ref)
+    assert_parity(got, ref, tag=f"configs[{config}] {name}, first {nseq} sequences ({int(offs[-1])} tokens)")
 
 
 def test_edge_lengths(model_path):
@@ -407,48 +424,69 @@ def test_multi_device_sharding(model_path, ndev):
 
 # ------------------------------------------------------------ op sweep -----
 
-@pytest.mark.parametrize("qtype", [synth.GGML_Q8_0, synth.GGML_Q6_K, synth.GGML_Q5_K, synth.GGML_Q4_K])
-@pytest.mark.parametrize("M,K,N", [(8, 768, 2304), (512, 3072, 768), (37, 768, 3072)])
+QTYPES = [synth.GGML_Q8_0, synth.GGML_Q6_K, synth.GGML_Q5_K, synth.GGML_Q4_K]
+SWEEP_KN = [(K, N) for K in (768, 3072) for N in (768, 2304, 3072)]
+
+
+def _sweep_weight(qtype, K, N):
+    rng = np.random.default_rng([0, qtype, K, N])
+    w = rng.standard_normal((N, K), dtype=np.float32) * np.float32(0.02)
+    return synth.quantize(w, qtype)
+
+
+def _row_parity(got, ref, tag):
+    """Per output row cosine >= 0.99999 and max |diff| <= 4e-3 * rms(ref):
+    fp16 operand rounding of x and W against the float32 reference."""
+    rms = float(np.sqrt((ref.astype(np.float64) ** 2).mean()))
+    err = float(np.abs(got - ref).max())
+    cos = (got * ref).sum(1) / (np.linalg.norm(got, axis=1) * np.linalg.norm(ref, axis=1))
+    log_parity(tag, min_cos=float(cos.min()), max_abs=err, max_abs_over_rms=err / rms)
+    assert err <= 4e-3 * rms, f"max |diff| {err:.3e} vs rms {rms:.3e}"
+    assert cos.min() >= COS_MIN, f"min cosine {cos.min():.8f}"
+
+
+@pytest.mark.parametrize("qtype", QTYPES)
+@pytest.mark.parametrize("M", [8, 512])
+@pytest.mark.parametrize("K,N", SWEEP_KN)
 def test_qgemm_vs_oracle(qtype, M, K, N):
-    """configs[1] op sweep at oracle-sized M: le_qgemm against the
-    reference's prepacked GEMM (gemm_avx512.go:67) and fused MatMulBatch
-    (ops.go:418).  Tolerance: per output row cosine >= 0.99999 and
-    max |diff| <= 4e-3 * rms(reference) (fp16 operand rounding)."""
-    rng = np.random.default_rng([0, qtype, M, K, N])
-    w = (rng.standard_normal((N, K), dtype=np.float32) * np.float32(0.02))
-    wq = synth.quantize(w, qtype)
-    x = rng.standard_normal((M, K), dtype=np.float32)
+    """configs[1] op sweep at the oracle-sized M (8, 512) for every K, N and
+    type: le_qgemm against the reference's prepacked GEMM
+    (gemm_avx512.go:67) and its fused MatMulBatch (ops.go:418)."""
+    wq = _sweep_weight(qtype, K, N)
+    x = np.random.default_rng([1, qtype, M, K, N]).standard_normal((M, K), dtype=np.float32)
     got = qgemm(qtype, wq, N, K, x)
     wd = oracle.dequant_matrix(qtype, wq, K, N)
-    for ref in (oracle.gemm(x, wd, NTHREADS), oracle.matmul_batch(qtype, wq, K, N, x, NTHREADS)):
-        rms = float(np.sqrt((ref ** 2).mean()))
-        assert np.abs(got - ref).max() <= 4e-3 * rms
-        cos = (got * ref).sum(1) / (np.linalg.norm(got, axis=1) * np.linalg.norm(ref, axis=1))
-        assert cos.min() >= COS_MIN
+    _row_parity(got, oracle.gemm(x, wd, NTHREADS), f"configs[1] type {qtype} M={M} K={K} N={N} vs prepacked gemm")
+    _row_parity(got, oracle.matmul_batch(qtype, wq, K, N, x, NTHREADS),
+                f"configs[1] type {qtype} M={M} K={K} N={N} vs MatMulBatch")
 
 
-def test_qgemm_full_size_vs_torch():
-    """configs[1] at M=32768 (too large for the oracle): the device result
-    against a torch float32 matmul of the exact dequantised weight."""
+@pytest.mark.parametrize("qtype", QTYPES)
+@pytest.mark.parametrize("K,N", SWEEP_KN)
+def test_qgemm_full_size_vs_torch(qtype, K, N):
+    """configs[1] at M=32768 (too large for the oracle) for every K, N and
+    type: the device result against a torch float32 matmul of the oracle's
+    exact dequantised weight."""
     import torch
-    qtype, M, K, N = synth.GGML_Q8_0, 32768, 3072, 3072
-    rng = np.random.default_rng(1)
-    w = rng.standard_normal((N, K), dtype=np.float32) * np.float32(0.02)
-    wq = synth.quantize(w, qtype)
-    x = torch.randn(M, K, device="cuda", generator=torch.Generator("cuda").manual_seed(0))
+    M = 32768
+    wq = _sweep_weight(qtype, K, N)
+    x = torch.randn(M, K, device="cuda", generator=torch.Generator("cuda").manual_seed(K + N))
     y = torch.empty(M, N, device="cuda")
     qw = QWeight(qtype, wq, N, K)
     try:
         qw.matmul_device(x.data_ptr(), M, y.data_ptr())
-        torch.cuda.synchronize()
+        qw.sync()
     finally:
         qw.close()
     wd = torch.from_numpy(oracle.dequant_matrix(qtype, wq, K, N)).cuda()
-    ref = x @ wd.T
-    rms = ref.pow(2).mean().sqrt().item()
-    assert (y - ref).abs().max().item() <= 4e-3 * rms
-    cos = torch.nn.functional.cosine_similarity(y, ref, dim=1)
-    assert cos.min().item() >= COS_MIN
+    ref = torch.matmul(x, wd.T)
+    rms = ref.double().pow(2).mean().sqrt().item()
+    err = (y - ref).abs().max().item()
+    cos = torch.nn.functional.cosine_similarity(y, ref, dim=1).min().item()
+    log_parity(f"configs[1] type {qtype} M={M} K={K} N={N} vs torch fp32", min_cos=cos, max_abs=err,
+               max_abs_over_rms=err / rms)
+    assert err <= 4e-3 * rms
+    assert cos >= COS_MIN
 
 
 @pytest.mark.parametrize("qtype", [synth.GGML_Q8_0, synth.GGML_Q4_K, synth.GGML_Q6_K])

@@ -2,7 +2,8 @@
 
 The no-alloc entry point keeps its scratch in one file-scope device array
 shared by every call on a device; two calls in a row with different shapes
-must each match the allocating entry point on the same weight and input.
+must each match the allocating entry point on the same weight and input, and
+the calls must leave the device's free memory unchanged.
 """
 import numpy as np
 import pytest
@@ -38,7 +39,7 @@ def test_noalloc_matches_qgemm_device_two_calls(qtype, N, K):
             got = torch.full((M, N), float("nan"), device="cuda")
             torch.cuda.synchronize()
             qw.matmul_device(x.data_ptr(), M, ref.data_ptr())
-            torch.cuda.synchronize()
+            qw.sync()
             qw.matmul_device_noalloc(x.data_ptr(), M, got.data_ptr())
             torch.cuda.synchronize()
             assert torch.isfinite(got).all()
@@ -65,9 +66,42 @@ def test_noalloc_rejects_oversize():
         got = torch.empty(M, 256, device="cuda")
         torch.cuda.synchronize()
         qw.matmul_device(x.data_ptr(), M, ref.data_ptr())
-        torch.cuda.synchronize()
+        qw.sync()
         qw.matmul_device_noalloc(x.data_ptr(), M, got.data_ptr())
         torch.cuda.synchronize()
         torch.testing.assert_close(got, ref, rtol=1e-6, atol=1e-6)
     finally:
         qw.close()
+
+
+def test_noalloc_leaves_free_memory_unchanged():
+    """The entry point's contract: no device allocation.  After every kernel
+    it launches has run once (module loading allocates on first use), calls
+    at the largest allowed M and at a new, smaller shape on a weight that
+    never ran le_qgemm_device leave cudaMemGetInfo's free bytes unchanged,
+    while le_qgemm_device on a fresh weight grows its own buffer."""
+    K, N = 768, 512
+    Mmax = QWeight.NOALLOC_MAX_ELEMS // K
+    warm = _weight(synth.GGML_Q8_0, N, K, seed=7)
+    fresh = _weight(synth.GGML_Q8_0, N, K, seed=8)
+    probe = _weight(synth.GGML_Q8_0, N, K, seed=9)
+    try:
+        x = _x(Mmax, K, 9)
+        y = torch.empty(Mmax, N, device="cuda")
+        for M in (Mmax, 100, 40):  # fp16 TMA, in-smem dequant and CUDA-core paths
+            warm.matmul_device_noalloc(x.data_ptr(), M, y.data_ptr())
+        torch.cuda.synchronize()
+        free0 = torch.cuda.mem_get_info()[0]
+        for M in (Mmax, 77, 40, Mmax):
+            fresh.matmul_device_noalloc(x.data_ptr(), M, y.data_ptr())
+        torch.cuda.synchronize()
+        assert torch.cuda.mem_get_info()[0] == free0
+        # The allocating entry point on a weight that has not run yet grows
+        # its fp16 input buffer (M*K*2 = 8 MiB here), which free memory shows.
+        probe.matmul_device(x.data_ptr(), Mmax, y.data_ptr())
+        probe.sync()
+        assert torch.cuda.mem_get_info()[0] < free0
+    finally:
+        warm.close()
+        fresh.close()
+        probe.close()
