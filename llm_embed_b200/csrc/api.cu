@@ -123,6 +123,8 @@ struct HostBuf {
 // A repacked projection weight.
 struct QMat {
   DevBuf buf;      // tile-blocked quantised weight (common.cuh)
+  DevBuf r16;      // the same bytes in 16-row tiles (gemm_r16.cuh) for few tokens
+  int r16_tiles = 0;
   DevBuf w16;      // its fp16 operand values [n_virt][K] for the large-batch GEMM
   int type = 0;   // GGML type
   int qf = 0;     // QFmt
@@ -226,7 +228,7 @@ struct le_model {
   long emb_row_bytes = 0;
   int vocab = 0;
   DevBuf emb, type0, embd_w, embd_b, rope_cos, rope_sin, status;
-  DevBuf barrier;  // arrival counter of the single-kernel small forward
+  DevBuf barrier;  // hand-off counters of the single-kernel small forward
   int sms = 0;
   std::vector<Layer> layers;
   cudaStream_t stream = nullptr;
@@ -335,7 +337,19 @@ static int make_qmat(QMat& q, int type, const void* src0, const void* src1, int 
   CK(launch_expand_f16(q.qf, q.buf.as<uint8_t>(), q.n_virt, K, q.w16.as<__half>(), s));
   CK(cudaStreamSynchronize(s));
   lt->expand_ms += now_ms() - t0;
+  t0 = now_ms();
+  q.r16_tiles = interleave ? (N + 7) / 8 : (N + 15) / 16;
+  TRY(q.r16.ensure((size_t)q.r16_tiles * (K / TILE_K) * (1024 + 16 * (q.qf == QF_Q8_0 ? 4 : 16))));
+  CK(launch_repack_r16(q.qf, q.buf.as<uint8_t>(), K, interleave ? 1 : 0, q.r16_tiles, q.r16.as<uint8_t>(), s));
+  CK(cudaStreamSynchronize(s));
+  lt->repack_ms += now_ms() - t0;
   return LE_OK;
+}
+
+// The layouts of a weight as the GEMM dispatch takes them (n_rows: the rows
+// the GEMM covers).
+static GemmW gemm_w(const QMat& q, int n_rows) {
+  return GemmW{q.qf, q.buf.as<uint8_t>(), q.r16.as<uint8_t>(), q.w16.as<__half>(), n_rows, q.r16_tiles, q.K};
 }
 
 static int upload_f32(DevBuf& b, const le_tensor_desc* t, int n, cudaStream_t s) {
@@ -420,8 +434,7 @@ static int ws_order_end(le_model* m, cudaStream_t s, bool capturing) {
 
 static int gemm(le_model* m, int cls, const QMat& W, const __half* A, int lda, const EpiParams& ep, cudaStream_t s) {
   m->prof.begin(cls, s);
-  CK(launch_gemm(W.qf, W.buf.as<uint8_t>(), W.w16.as<__half>(), W.n_virt, W.K, A, lda, ep, m->status.as<DevStatus>(),
-                 s));
+  CK(launch_gemm(gemm_w(W, W.n_virt), A, lda, ep, m->status.as<DevStatus>(), s));
   m->prof.end(s);
   return LE_OK;
 }
@@ -471,18 +484,19 @@ static int forward(le_model* m, const int32_t* d_ids, const int32_t* d_offsets, 
     sp.pos = pos;
     sp.qkv = qkv;
     sp.att = att;
-    sp.y = y32;
+    sp.y1 = y32;
+    sp.y2 = y32 + (size_t)SMALL_MAX_TOKENS * H;
     sp.ff = ff;
     sp.h_out = h32;
-    sp.barrier = m->barrier.as<unsigned>();
+    sp.sync = m->barrier.as<unsigned>();
     sp.status = m->status.as<DevStatus>();
     for (int l = 0; l < sp.n_layers; l++) {
       const Layer& L = m->layers[l];
       const QMat* q[4] = {&L.qkv, &L.out, &L.upgate, &L.down};
       const int modes[4] = {EPI_QKV, EPI_F32, EPI_GEGLU, EPI_F32};
       for (int i = 0; i < 4; i++)
-        sp.layers[l].g[i] = SmallGemm{q[i]->qf == QF_F16 ? nullptr : q[i]->buf.as<uint8_t>(), q[i]->qf, q[i]->K,
-                                      q[i]->n_virt / 2, modes[i]};
+        sp.layers[l].g[i] = SmallGemm{q[i]->qf == QF_F16 ? nullptr : q[i]->r16.as<uint8_t>(), q[i]->qf, q[i]->K,
+                                      q[i]->r16_tiles, modes[i]};
       sp.layers[l].attn_w = L.attn_w.as<float>();
       sp.layers[l].attn_b = L.attn_b.as<float>();
       sp.layers[l].out_w = L.out_w.as<float>();
@@ -818,7 +832,7 @@ static int load_impl(int dev, const le_tensor_desc* ts, int nt, const le_hparams
   CK(cudaStreamCreateWithFlags(&m->capture_stream, cudaStreamNonBlocking));
   CK(cudaEventCreateWithFlags(&m->ws_done, cudaEventDisableTiming));
   CK(cudaDeviceGetAttribute(&m->sms, cudaDevAttrMultiProcessorCount, dev));
-  TRY(m->barrier.ensure(16));
+  TRY(m->barrier.ensure(small_sync_bytes()));
   cudaStream_t s = m->stream;
   const int H = hp->hidden, F = hp->ffn;
   auto need = [&](const std::string& n) { return find(ts, nt, n); };
@@ -833,7 +847,9 @@ static int load_impl(int dev, const le_tensor_desc* ts, int nt, const le_hparams
   if (m->emb_row_bytes < 0) return fail(LE_EINVAL, "unsupported embedding type: %d", te->type);
   m->vocab = te->n_dims > 1 ? (int)te->dims[1] : 1;
   if (te->n_bytes < m->emb_row_bytes * m->vocab) return fail(LE_EINVAL, "token_embd.weight too short");
-  TRY(m->emb.ensure((size_t)m->emb_row_bytes * m->vocab));
+  // 16 spare bytes: the single-kernel forward stages rows with 16-byte loads
+  // from the 16-byte boundary below each row.
+  TRY(m->emb.ensure((size_t)m->emb_row_bytes * m->vocab + 16));
   {
     const double t0 = now_ms();
     CK(cudaMemcpyAsync(m->emb.p, te->data, (size_t)m->emb_row_bytes * m->vocab, cudaMemcpyHostToDevice, s));
@@ -977,7 +993,7 @@ int le_model_load_stats(const le_model* m, le_load_stats* out) {
   out->h2d_bytes = m->load.h2d_bytes;
   size_t dev_bytes = m->emb.n + m->type0.n + m->embd_w.n + m->embd_b.n + m->rope_cos.n + m->rope_sin.n;
   for (const Layer& L : m->layers) {
-    for (const QMat* q : {&L.qkv, &L.out, &L.upgate, &L.down}) dev_bytes += q->buf.n + q->w16.n;
+    for (const QMat* q : {&L.qkv, &L.out, &L.upgate, &L.down}) dev_bytes += q->buf.n + q->r16.n + q->w16.n;
     dev_bytes += L.attn_w.n + L.attn_b.n + L.out_w.n + L.out_b.n;
   }
   out->weight_bytes = (int64_t)dev_bytes;
@@ -1167,8 +1183,7 @@ int le_qgemm_device(le_qweight* w, const float* d_x, int M, float* d_y, void* st
   e.N = w->w.n_real;
   e.out32 = d_y;
   e.ldo = w->w.n_real;
-  CK(launch_gemm(w->w.qf, w->w.buf.as<uint8_t>(), w->w.w16.as<__half>(), w->w.n_real, K, w->x16.as<__half>(), K, e,
-                 w->status.as<DevStatus>(), s));
+  CK(launch_gemm(gemm_w(w->w, w->w.n_real), w->x16.as<__half>(), K, e, w->status.as<DevStatus>(), s));
   return LE_OK;
 }
 
@@ -1252,7 +1267,7 @@ int le_qgemm_device_noalloc(le_qweight* w, const float* d_x, int M, float* d_y, 
   e.N = w->w.n_real;
   e.out32 = d_y;
   e.ldo = w->w.n_real;
-  CK(launch_gemm(w->w.qf, w->w.buf.as<uint8_t>(), w->w.w16.as<__half>(), w->w.n_real, K, x16, K, e, st, s));
+  CK(launch_gemm(gemm_w(w->w, w->w.n_real), x16, K, e, st, s));
   DevStatus h{};
   CK(cudaMemcpyAsync(&h, st, sizeof h, cudaMemcpyDeviceToHost, s));
   CK(cudaStreamSynchronize(s));

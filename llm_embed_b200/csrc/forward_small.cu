@@ -1,73 +1,92 @@
-// The whole encoder forward for a few tokens in one persistent kernel.
+// The whole encoder forward for a few tokens (at most SMALL_MAX_TOKENS) in
+// one persistent kernel: one CTA per SM, all resident (cooperative launch).
 //
-// At batch 1 the forward pass is ~85 dependent steps whose work is tiny
-// (8 tokens) next to the weights they stream (120 MB for Q8_0), so separate
-// kernels leave the GPU idle between launches.  Here one CTA per SM runs all
-// layers (cooperative launch, so every CTA is resident), with a grid barrier
-// where a step needs another CTA's results:
+// At batch 1 the forward is a chain of small dependent steps over 120 MB of
+// weights (Q8_0).  Weights never depend on activations, so each CTA streams
+// the weight pages of its share of every step into a shared-memory ring
+// ahead of use (a producer warp issuing TMA bulk copies, mbarrier-tracked),
+// and the chain itself only waits for the activations other CTAs produce.
 //
-//   per layer:  [LN + QKV GEMM + RoPE] | [attention] | [out GEMM] |
-//               [LN + up/gate GEMM + GEGLU] | [down GEMM] |
+// Per layer, CTA c:
+//   QKV     LayerNorm of its own copy of the residual stream (every CTA holds
+//           h and applies each LayerNorm itself, in one fixed order, so all
+//           copies are equal), then its 16-row QKV tile(s) with RoPE
+//   ATT     (12 CTAs, one per head) once the head's 12 QKV tiles are done:
+//           attention of every sequence for that head
+//   OUT     (48 CTAs) once all heads are done: an output-projection tile
+//   UG      every CTA, once all output tiles are done: LayerNorm, then its
+//           2-3 up/gate tiles with GEGLU
+//   DOWN    (48 CTAs) once every CTA finished UG: a down-projection tile
+// Each hand-off is a release-add on a counter after the producing tile's
+// stores and an acquire poll by the consumers (bounded: WAIT_LIMIT_NS, then
+// DE_TIMEOUT and every CTA leaves); there is no grid-wide barrier.
 //
-// * The residual stream h (T x 768 float32) lives in every CTA's shared
-//   memory: each CTA applies the residual LayerNorms (bert.go:262-280)
-//   itself, in the same order, so all copies hold the same values and a
-//   LayerNorm needs no barrier.
-// * Each GEMM's output row pairs are split evenly over the CTAs.  A CTA's
-//   slice of the next GEMM's tile-blocked quantised weight (quant bytes +
-//   scales, up to ~41 KB) is prefetched into shared memory with cp.async
-//   while the current step and its barrier run, and dequantised there to the
-//   same fp16 operand values as every other GEMM path.
-// * Attention runs one warp per (sequence, head) with the same tensor-core
-//   tile code as the attention kernels (attention_tile.cuh), so a sequence
-//   gets the same bits here as in a larger batch through the separate
-//   kernels.
-//
-// Barriers are a global arrival counter (zeroed before the launch) polled
-// with acquire loads; every wait is bounded by WAIT_LIMIT_NS and reports
-// DE_TIMEOUT through the status word, after which all CTAs leave.
+// The GEMM tiles run the row16 mma.sync primitive of gemm_r16.cuh with the
+// same K split and reduction order as the small-batch GEMM kernel, and
+// attention the warp tile of attention_tile.cuh as the attention kernels do,
+// so a sequence gets the same bits here as in a batch of up to 63 tokens.
 #include "attention_tile.cuh"
-#include "dequant.cuh"
-#include "epilogue.cuh"
+#include "gemm_r16.cuh"
 #include "gguf_decode.cuh"
 #include "kernels.h"
 #include "ln_warp.cuh"
+#include "tcgen05.cuh"
 
 #include <mutex>
 
 namespace le {
 namespace fs {
 
+using tcx::bulk_load;
+using tcx::mbar_arrive;
+using tcx::mbar_expect_tx;
+using tcx::mbar_init;
+using tcx::mbar_wait;
+
 constexpr int H = SMALL_HIDDEN;
 constexpr int F = SMALL_FFN;
 constexpr int HEADS = SMALL_HEADS;
 constexpr int HD = H / HEADS;
-constexpr int TS = SMALL_MAX_TOKENS;
-constexpr int NTHREADS = 256;
-constexpr int NWARPS = NTHREADS / 32;
+constexpr int NCW = r16::WARPS;            // compute warps
+constexpr int NTHREADS = (NCW + 1) * 32;   // + the producer warp
+constexpr int NCT = NCW * 32;              // compute threads (named barrier 1)
+constexpr int LDX = H + 8;                 // padded fp16 row stride of x
+constexpr int PAGE_COLS = 768;             // a page: 16 rows x 768 columns of one tile
+constexpr int PAGE_CHUNKS = PAGE_COLS / TILE_K;
+constexpr int SLOT = PAGE_CHUNKS * r16::chunk_bytes(QF_KMIN);  // 15,360 B: the largest page
+constexpr int ATT_WARP_BYTES = 3 * 16 * attn::LDS * 2;
+constexpr int SMEM_MAX = 232448;
+constexpr int MAX_SLOTS = 16;
+constexpr int MAX_TILES = 3;               // tiles of one step per CTA (up/gate: 384 over 148 CTAs)
 
-// Weight slice of one GEMM step in shared memory: for each local pair j,
-// k-step ks and row (a, b): 64 quant bytes, then (after all of them) MB
-// bytes of scales per (j, ks, row).
-__host__ __device__ constexpr int meta_row_bytes(int qf) { return qf == QF_Q8_0 ? 4 : 16; }
-constexpr int WBUF_BYTES = 41472;  // 40.5 KB: the largest slice (K-quant up/gate, 21 pairs) is 40,320 B
+// Hand-off counters (zeroed before each launch), one 128-byte line each.
+constexpr int CNT_STRIDE = 32;
+constexpr int CNT_QKV = 0;  // + head: QKV tiles done
+constexpr int CNT_ATT = HEADS;
+constexpr int CNT_Y1 = HEADS + 1;
+constexpr int CNT_FF = HEADS + 2;
+constexpr int CNT_Y2 = HEADS + 3;
+constexpr int N_CNT = HEADS + 4;
 
-// Shared memory: two weight slice buffers; the residual stream h; and one
-// region U used by one step at a time: the LN output x [T][H] fp16 (QKV,
-// up/gate), the attention staging, the attention output [T][H] (out
-// projection) or the GEGLU output [T][F] (down projection), staged once per
-// step so the GEMM reads its input from shared memory.
-struct SmemLayout {
-  static constexpr int OFF_W = 0;
-  static constexpr int OFF_H = OFF_W + 2 * WBUF_BYTES;                 // float h[TS][H]
-  static constexpr int ATT_WARP_BYTES = 3 * 16 * attn::LDS * 2;       // half Q, K, V [16][LDS] per warp
-  static constexpr int U_BYTES = (TS * F * 2 > NWARPS * ATT_WARP_BYTES) ? TS * F * 2 : NWARPS * ATT_WARP_BYTES;
-  static constexpr int OFF_U = OFF_H + TS * H * 4;
-  static constexpr int OFF_TOK = OFF_U + U_BYTES;                      // int pos[TS] (and spare)
-  static constexpr int OFF_MISC = OFF_TOK + 4 * TS * 4;                // int flag
-  static constexpr int BYTES = OFF_MISC + 16;
+template <int NT>
+struct Lay {
+  static constexpr int TS = 8 * NT;
+  static constexpr int H_BYTES = TS * H * 4;
+  static constexpr int X_BYTES = TS * LDX * 2;
+  static constexpr int U_BYTES = X_BYTES > NCW * ATT_WARP_BYTES ? X_BYTES : NCW * ATT_WARP_BYTES;
+  static constexpr int RED_BYTES = MAX_TILES * NCW * NT * 32 * 16;
+  static constexpr int FIXED = H_BYTES + U_BYTES + RED_BYTES + 2 * MAX_SLOTS * 8 + 64;
+  static constexpr int R = (SMEM_MAX - FIXED) / SLOT < MAX_SLOTS ? (SMEM_MAX - FIXED) / SLOT : MAX_SLOTS;
+  static constexpr int OFF_RING = 0;
+  static constexpr int OFF_H = R * SLOT;
+  static constexpr int OFF_U = OFF_H + H_BYTES;
+  static constexpr int OFF_RED = OFF_U + U_BYTES;
+  static constexpr int OFF_BAR = OFF_RED + RED_BYTES;  // full[R], empty[R]
+  static constexpr int OFF_MISC = OFF_BAR + 2 * R * 8;
+  static constexpr int BYTES = OFF_MISC + 64;
+  static_assert(R >= 5, "the ring must hold a 4-page tile and the next page");
+  static_assert(BYTES <= SMEM_MAX, "shared memory budget");
 };
-static_assert(SmemLayout::BYTES <= 232448, "shared memory budget");
 
 __device__ __forceinline__ unsigned ld_acquire(const unsigned* p) {
   unsigned v;
@@ -77,106 +96,85 @@ __device__ __forceinline__ unsigned ld_acquire(const unsigned* p) {
 __device__ __forceinline__ void red_release_add(unsigned* p, unsigned v) {
   asm volatile("red.release.gpu.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
+// Barrier of the compute warps only (the producer warp never joins it).
+__device__ __forceinline__ void bar_compute() { asm volatile("bar.sync 1, %0;" ::"n"(NCT) : "memory"); }
 
-// Grid barrier number `k` (0, 1, ...): returns false in every thread of the
-// CTA if the wait timed out or another CTA reported a failure.
-__device__ bool grid_sync(unsigned* counter, unsigned k, DevStatus* st, int* flag) {
-  __syncthreads();
+// Tiles [t0, t1) of step m for CTA c: an even split, the down projection's
+// shifted by half the grid so its CTAs are not the output projection's.
+__device__ __forceinline__ void tile_range(int m, int n_tiles, int* t0, int* t1) {
+  const int G = gridDim.x;
+  const int c = m == 3 ? (int)((blockIdx.x + G / 2) % G) : (int)blockIdx.x;
+  *t0 = (int)((long)n_tiles * c / G);
+  *t1 = (int)((long)n_tiles * (c + 1) / G);
+}
+__device__ __forceinline__ int att_cta(int head) { return (int)((long)head * gridDim.x / HEADS); }
+__device__ __forceinline__ int pages_of(const SmallGemm& g) { return g.K / PAGE_COLS; }
+
+template <int R_>
+struct SharedT {
+  static constexpr int R = R_;
+  uint8_t* ring;
+  float* h;
+  __half* x;
+  uint8_t* U;
+  float4* red;
+  uint32_t bar0;
+  volatile int* abort;
+  volatile int* flag;
+  int* pos;
+};
+
+// Compute threads: wait until *c >= target (thread 0 polls with acquire
+// loads; the others learn the outcome at the barrier).  False if the wait
+// timed out or another CTA reported a failure.
+template <class SH>
+__device__ bool wait_cnt(const SmallParams& p, const SH& S, int idx, unsigned target, int site) {
   if (threadIdx.x == 0) {
-    *flag = 1;
-    // The release orders the CTA's writes (made visible to this thread by
-    // the barrier above) before the arrival; the acquire loads below order
-    // every later read after the other CTAs' arrivals.
-    red_release_add(counter, 1u);
-    const unsigned target = (k + 1) * gridDim.x;
-    if (ld_acquire(counter) < target) {
+    const unsigned* c = p.sync + idx * CNT_STRIDE;
+    int ok = !*S.abort;
+    if (ok && ld_acquire(c) < target) {
       const uint64_t t0 = globaltimer_ns();
       for (uint32_t i = 1;; i++) {
-        if (ld_acquire(counter) >= target) break;
+        if (ld_acquire(c) >= target) break;
         if ((i & 63) == 0) {
-          if (ld_acquire(reinterpret_cast<const unsigned*>(&st->code)) != 0) {
-            *flag = 0;
+          if (ld_acquire(reinterpret_cast<const unsigned*>(&p.status->code)) != 0) {
+            ok = 0;
             break;
           }
           if (globaltimer_ns() - t0 > WAIT_LIMIT_NS) {
-            report(st, DE_TIMEOUT, 40 + (int)(k % 10), (int)blockIdx.x);
-            *flag = 0;
+            report(p.status, DE_TIMEOUT, site, (int)blockIdx.x);
+            ok = 0;
             break;
           }
         }
       }
     }
+    if (!ok) *S.abort = 1;
+    *S.flag = ok;
   }
-  __syncthreads();
-  return *reinterpret_cast<volatile int*>(flag) != 0;
+  bar_compute();
+  return *S.flag != 0;
 }
 
-__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src) {
-  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src) : "memory");
-}
-__device__ __forceinline__ void cp_async4(uint32_t dst, const void* src) {
-  asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(dst), "l"(src) : "memory");
-}
-__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
-__device__ __forceinline__ void cp_async_wait1() { asm volatile("cp.async.wait_group 1;" ::: "memory"); }
-
-__device__ __forceinline__ float warp_sum(float v) {
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-  return v;
-}
-
-// Output pairs [p0, p1) of a GEMM with `n_pairs` pairs for this CTA.
-__device__ __forceinline__ void pair_range(int n_pairs, int* p0, int* p1) {
-  *p0 = (int)((long)n_pairs * blockIdx.x / gridDim.x);
-  *p1 = (int)((long)n_pairs * (blockIdx.x + 1) / gridDim.x);
-}
-
-// Issue (no wait) the cp.async copies of this CTA's slice of GEMM `g`.
-__device__ void prefetch_slice(const SmallGemm& g, uint32_t buf) {
-  const int ksteps = g.K / TILE_K;
-  const int cb = chunk_bytes(g.qf), mb = meta_row_bytes(g.qf);
-  int p0, p1;
-  pair_range(g.n_pairs, &p0, &p1);
-  const int units = (p1 - p0) * ksteps * 2;  // (pair, k-step, row)
-  const uint32_t meta0 = buf + units * 64;
-  for (int u = threadIdx.x; u < units * 5; u += NTHREADS) {
-    const int unit = u / 5, part = u % 5;
-    const int which = unit & 1, ks = (unit >> 1) % ksteps, j = (unit >> 1) / ksteps;
-    int ra, rb;
-    pair_rows(g.mode, p0 + j, &ra, &rb);
-    const int row = which ? rb : ra;
-    const uint8_t* chunk = g.w + ((long)(row / TILE_N) * ksteps + ks) * cb;
-    const int r = row % TILE_N;
-    if (part < 4) {
-      cp_async16(buf + unit * 64 + part * 16, chunk + r * TILE_K + part * 16);
-    } else if (mb == 16) {
-      cp_async16(meta0 + unit * 16, chunk + TILE_Q_BYTES + r * 16);
-    } else {
-      cp_async4(meta0 + unit * 4, chunk + TILE_Q_BYTES + r * 4);
-    }
-  }
-}
-
-__device__ __forceinline__ void h8_to_f32(uint4 h, float* f) {
-  const __half2* p = reinterpret_cast<const __half2*>(&h);
-#pragma unroll
-  for (int i = 0; i < 4; i++) {
-    const float2 v = __half22float2(p[i]);
-    f[2 * i] = v.x;
-    f[2 * i + 1] = v.y;
-  }
+// Compute threads: after this CTA's stores of a hand-off, add 1 to counter idx.
+__device__ __forceinline__ void signal(const SmallParams& p, int idx) {
+  bar_compute();
+  if (threadIdx.x == 0) red_release_add(p.sync + idx * CNT_STRIDE, 1u);
 }
 
 // LayerNorm (ops_simd.go:7-24) of h[t] (+ y[t] when y) into h[t] and its fp16
-// copy x[t]; one warp per token row, single-pass sum/sumSq in float32.
+// copy x[t]; one warp per token row (ln_row_stats order).  Every global load
+// (y, gamma, beta) is issued before the statistics, so the row waits for one
+// memory round trip.
 __device__ void ln_rows(float* h, __half* x, const float* y, const float* w, const float* b, float eps, int T) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  for (int t = warp; t < T; t += NWARPS) {
-    float4 v[H / 128];
+  for (int t = warp; t < T; t += NCW) {
+    float4 v[H / 128], wv[H / 128], bv[H / 128];
 #pragma unroll
     for (int i = 0; i < H / 128; i++) {
       const int c = (i * 32 + lane) * 4;
+      wv[i] = __ldg(reinterpret_cast<const float4*>(w + c));
+      bv[i] = __ldg(reinterpret_cast<const float4*>(b + c));
       float4 a = *reinterpret_cast<const float4*>(h + t * H + c);
       if (y) {
         const float4 d = __ldcg(reinterpret_cast<const float4*>(y + (long)t * H + c));
@@ -189,145 +187,104 @@ __device__ void ln_rows(float* h, __half* x, const float* y, const float* w, con
 #pragma unroll
     for (int i = 0; i < H / 128; i++) {
       const int c = (i * 32 + lane) * 4;
-      const float4 o = ln_apply(v[i], mean, inv, *reinterpret_cast<const float4*>(w + c),
-                                *reinterpret_cast<const float4*>(b + c));
+      const float4 o = ln_apply(v[i], mean, inv, wv[i], bv[i]);
       *reinterpret_cast<float4*>(h + t * H + c) = o;
       uint2 hh;
       hh.x = pack_half2(o.x, o.y);
       hh.y = pack_half2(o.z, o.w);
-      *reinterpret_cast<uint2*>(x + t * H + c) = hh;
+      *reinterpret_cast<uint2*>(x + t * LDX + c) = hh;
     }
   }
 }
 
-// Embedding rows (bert.go:227-247): token_embd row + token_types row 0.
-__device__ void embed_rows(const SmallParams& p, float* h, int T) {
-  for (int i = threadIdx.x; i < T * H; i += NTHREADS) {
-    const int t = i / H, c = i % H;
-    int id = p.ids[t];
-    if (id < 0 || id >= p.vocab) {
-      if (c == 0) report(p.status, DE_BOUNDS, 2, id);
-      id = 0;
-    }
-    h[i] = __fadd_rn(gguf_elem(p.emb_type, p.emb + (long)id * p.emb_row_bytes, c), p.type0[c]);
-  }
-}
-
-// Copy rows [0, T) x K of an fp16 activation written by other CTAs into
-// shared memory (cp.async through L2; the caller commits and waits).
-__device__ void stage_rows(uint32_t dst, const __half* src, int T, int K) {
-  const int n = T * K / 8;
-  for (int i = threadIdx.x; i < n; i += NTHREADS) cp_async16(dst + i * 16, src + (long)i * 8);
-}
-
-// Butterfly reduce-scatter of NV (16 or 32) per-lane partial sums: lane l
-// ends with the warp total of value l (NV = 32) or l / 2 (NV = 16).  Each
-// total is formed by the same pairings, own partial first, as a xor-butterfly
-// all-reduce of that value, so the bits equal warp_sum's.
-template <int NV>
-__device__ __forceinline__ float reduce_scatter(float (&v)[NV]) {
-  const int lane = threadIdx.x & 31;
+// Embedding rows (bert.go:227-247): token_embd row + token_types row 0.  The
+// rows' bytes are first staged into `stage` with 16-byte loads from the
+// 16-byte boundary at or below each row (all issued at once; the embedding
+// buffer carries 16 spare bytes), then decoded from shared memory.
+__device__ void embed_rows(const SmallParams& p, float* h, uint8_t* stage, int T) {
+  const int rb = (int)p.emb_row_bytes;
+  const int stride = (rb + 31) & ~15;  // staged bytes per row (multiple of 16)
+  const int n16 = stride / 16;
+  constexpr int PER = 8;  // loads in flight per thread before their stores
+  for (int i0 = threadIdx.x; i0 < T * n16; i0 += NCT * PER) {
+    uint4 v[PER];
 #pragma unroll
-  for (int o = 16, n = NV; n > 1; o >>= 1, n >>= 1) {
-    const bool hi = (lane & o) != 0;
-#pragma unroll
-    for (int i = 0; i < n / 2; i++) {
-      const float keep = hi ? v[i + n / 2] : v[i];
-      const float send = hi ? v[i] : v[i + n / 2];
-      v[i] = keep + __shfl_xor_sync(0xffffffffu, send, o);
-    }
-  }
-  if constexpr (NV == 16) v[0] += __shfl_xor_sync(0xffffffffu, v[0], 1);
-  return v[0];
-}
-
-// One GEMM step over this CTA's pairs: y = x . W^T for T <= TT tokens, x
-// fp16 [T][K] in shared memory, weights from the prefetched slice.  Lanes own
-// 16-column chunks (the accumulation order of gemm_simt.cu); the sums reduce
-// across the warp onto one lane per (row, token) and the epilogue runs for
-// all tokens at once.
-template <int QF, int TT>
-__device__ void gemm_step(const SmallGemm& g, const uint8_t* wbuf, const __half* x, int T, const EpiParams& ep) {
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int ksteps = g.K / TILE_K, nch = g.K / 16;
-  constexpr int MB = meta_row_bytes(QF);
-  int p0, p1;
-  pair_range(g.n_pairs, &p0, &p1);
-  const int units = (p1 - p0) * ksteps * 2;
-  const uint8_t* meta0 = wbuf + units * 64;
-  for (int j = warp; j < p1 - p0; j += NWARPS) {
-    float acc[2 * TT];  // [row][token]
-#pragma unroll
-    for (int i = 0; i < 2 * TT; i++) acc[i] = 0.f;
-    for (int c = lane; c < nch; c += 32) {
-      const int ks = c >> 2, part = c & 3;
-      const int ua = (j * ksteps + ks) * 2;
-      const uint4 qa = *reinterpret_cast<const uint4*>(wbuf + ua * 64 + part * 16);
-      const uint4 qb = *reinterpret_cast<const uint4*>(wbuf + (ua + 1) * 64 + part * 16);
-      float wa[16], wb[16];
-      h8_to_f32(dq8_f16<QF>(make_uint2(qa.x, qa.y), meta0 + ua * MB, 0, part * 2), wa);
-      h8_to_f32(dq8_f16<QF>(make_uint2(qa.z, qa.w), meta0 + ua * MB, 0, part * 2 + 1), wa + 8);
-      h8_to_f32(dq8_f16<QF>(make_uint2(qb.x, qb.y), meta0 + (ua + 1) * MB, 0, part * 2), wb);
-      h8_to_f32(dq8_f16<QF>(make_uint2(qb.z, qb.w), meta0 + (ua + 1) * MB, 0, part * 2 + 1), wb + 8);
-#pragma unroll
-      for (int t = 0; t < TT; t++) {
-        // Rows t >= T hold stale data; their sums are discarded.
-        const uint4* xp = reinterpret_cast<const uint4*>(x + (long)t * g.K + c * 16);
-        float xv[16];
-        h8_to_f32(xp[0], xv);
-        h8_to_f32(xp[1], xv + 8);
-#pragma unroll
-        for (int e = 0; e < 16; e++) {
-          acc[t] = fmaf(wa[e], xv[e], acc[t]);
-          acc[TT + t] = fmaf(wb[e], xv[e], acc[TT + t]);
-        }
+    for (int q = 0; q < PER; q++) {
+      const int i = i0 + q * NCT;
+      if (i < T * n16) {
+        const int t = i / n16, j = i % n16;
+        int id = p.ids[t];
+        if (id < 0 || id >= p.vocab) id = 0;
+        const uintptr_t a = reinterpret_cast<uintptr_t>(p.emb + (long)id * rb) & ~(uintptr_t)15;
+        v[q] = __ldg(reinterpret_cast<const uint4*>(a) + j);
       }
     }
-    const float v = reduce_scatter<2 * TT>(acc);
-    // Row a of token t sits on lane t (TT = 16) or 2t (TT = 8), row b 16 lanes up.
-    const float vb = __shfl_down_sync(0xffffffffu, v, 16);
-    const int t = TT == 16 ? lane : lane >> 1;
-    const bool mine = TT == 16 ? lane < 16 : (lane < 16 && (lane & 1) == 0);
-    if (mine && t < T) {
-      int ra, rb;
-      pair_rows(g.mode, p0 + j, &ra, &rb);
-      epi_pair(ep, t, ra, v, vb);
+#pragma unroll
+    for (int q = 0; q < PER; q++) {
+      const int i = i0 + q * NCT;
+      if (i < T * n16) *reinterpret_cast<uint4*>(stage + (i / n16) * stride + (i % n16) * 16) = v[q];
     }
   }
-}
-
-template <int TT>
-__device__ void gemm_tt(const SmallGemm& g, const uint8_t* wbuf, const __half* x, int T, const EpiParams& ep) {
-  switch (g.qf) {
-    case QF_Q8_0: gemm_step<QF_Q8_0, TT>(g, wbuf, x, T, ep); break;
-    case QF_KMIN: gemm_step<QF_KMIN, TT>(g, wbuf, x, T, ep); break;
-    default: gemm_step<QF_Q6K, TT>(g, wbuf, x, T, ep); break;
+  bar_compute();
+  for (int i = threadIdx.x; i < T * H; i += NCT) {
+    const int t = i / H, c = i % H;
+    const int id = p.ids[t];
+    if (id < 0 || id >= p.vocab) {
+      if (c == 0) report(p.status, DE_BOUNDS, 2, id);
+    }
+    const int sid = (id < 0 || id >= p.vocab) ? 0 : id;
+    const int mis = (int)(reinterpret_cast<uintptr_t>(p.emb + (long)sid * rb) & 15);
+    h[i] = __fadd_rn(gguf_elem(p.emb_type, stage + t * stride + mis, c), p.type0[c]);
   }
 }
-__device__ void gemm_any(const SmallGemm& g, const uint8_t* wbuf, const __half* x, int T, const EpiParams& ep) {
-  if (T <= 8) gemm_tt<8>(g, wbuf, x, T, ep);
-  else gemm_tt<16>(g, wbuf, x, T, ep);
+
+// L2 prefetch of the small per-layer tensors the chain reads after waits (the
+// LayerNorm vectors, the RoPE rows of the call's positions), spread over the
+// CTAs, so those reads hit L2 instead of DRAM.
+__device__ void prefetch_small(const SmallParams& p) {
+  const int G = gridDim.x;
+  const int per_layer = 4 * (H * 4 / 128);  // 128-byte lines of the four vectors
+  for (int i = blockIdx.x * NCT + threadIdx.x; i < p.n_layers * per_layer; i += G * NCT) {
+    const int l = i / per_layer, r = i % per_layer, v = r / (H * 4 / 128), line = r % (H * 4 / 128);
+    const SmallLayer& L = p.layers[l];
+    const float* base = v == 0 ? L.attn_w : v == 1 ? L.attn_b : v == 2 ? L.out_w : L.out_b;
+    asm volatile("prefetch.global.L2 [%0];" ::"l"(base + line * 32));
+  }
+  if (blockIdx.x == 0 && threadIdx.x < p.T) {
+    const int t = threadIdx.x;
+    int s = 0;
+    while (s + 1 < p.nseq && p.offsets[s + 1] <= t) s++;
+    const int pos = t - p.offsets[s];
+    asm volatile("prefetch.global.L2 [%0];" ::"l"(p.rope_cos + pos * (HD / 2)));
+    asm volatile("prefetch.global.L2 [%0];" ::"l"(p.rope_sin + pos * (HD / 2)));
+  }
 }
 
-// Attention (bert.go:356-402) for (sequence, head) units, one warp each:
-// the unit's Q, K, V rows (written by other CTAs, read through L2) into the
+// Attention (bert.go:356-402) of head `head` for every sequence, one warp per
+// sequence: its Q, K, V rows (from other CTAs, read through L2) into the
 // warp's staging area, zero past the sequence, then the shared warp tile.
-__device__ void attention_step(const SmallParams& p, uint8_t* att_smem) {
+__device__ void attention_head(const SmallParams& p, uint8_t* U, int head) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int gw = blockIdx.x * NWARPS + warp, nw = gridDim.x * NWARPS;
-  __half(*sQ)[attn::LDS] = reinterpret_cast<__half(*)[attn::LDS]>(att_smem + warp * SmemLayout::ATT_WARP_BYTES);
+  __half(*sQ)[attn::LDS] = reinterpret_cast<__half(*)[attn::LDS]>(U + warp * ATT_WARP_BYTES);
   __half(*sK)[attn::LDS] = sQ + 16;
   __half(*sV)[attn::LDS] = sK + 16;
-  for (int u = gw; u < p.nseq * HEADS; u += nw) {
-    const int s = u / HEADS, head = u % HEADS;
+  for (int s = warp; s < p.nseq; s += NCW) {
     const int t0 = p.offsets[s], L = p.offsets[s + 1] - t0;
     if (L == 0) continue;
-    for (int i = lane; i < 3 * 16 * 8; i += 32) {
-      const int which = i >> 7, r = (i >> 3) & 15, c = (i & 7) * 8;
-      uint4 v = make_uint4(0, 0, 0, 0);
-      if (r < L)
-        v = __ldcg(reinterpret_cast<const uint4*>(p.qkv + (long)(t0 + r) * 3 * H + which * H + head * HD + c));
-      *reinterpret_cast<uint4*>(&sQ[which * 16 + r][c]) = v;
+    // All twelve 16-byte loads of the lane first, then the stores (the
+    // shared-memory stores go through generic pointers, which the compiler
+    // cannot separate from the global loads).
+    uint4 v[12];
+#pragma unroll
+    for (int j = 0; j < 12; j++) {
+      const int i = lane + 32 * j, which = i >> 7, r = (i >> 3) & 15, c = (i & 7) * 8;
+      v[j] = r < L ? __ldcg(reinterpret_cast<const uint4*>(p.qkv + (long)(t0 + r) * 3 * H + which * H + head * HD + c))
+                   : make_uint4(0, 0, 0, 0);
+    }
+#pragma unroll
+    for (int j = 0; j < 12; j++) {
+      const int i = lane + 32 * j, which = i >> 7, r = (i >> 3) & 15, c = (i & 7) * 8;
+      *reinterpret_cast<uint4*>(&sQ[which * 16 + r][c]) = v[j];
     }
     __syncwarp();
     attn::attn_rows16(sQ, 0, sK, sV, L, p.att + (long)t0 * H + head * HD, H, 0);
@@ -335,56 +292,218 @@ __device__ void attention_step(const SmallParams& p, uint8_t* att_smem) {
   }
 }
 
+// Tiles t0 .. t0+nt-1 (nt <= MAX_TILES) of step g, whose pages sit at ring
+// positions seq0.. of the page sequence: every warp runs its units of every
+// tile (the B operand fragments loaded once per unit and shared by the
+// tiles), then the partials, the reduction and the epilogue of all tiles.
+// B operand: x in shared memory (xs, stride LDX) or a global fp16 matrix
+// (xg, stride ldg; all of the warp's fragments are loaded before the first
+// MMA, one memory round trip).  For EPI_QKV the RoPE cos/sin of each output
+// item come preloaded in rc/rs (item i < 64 NT of the first tile).  Returns
+// false if a page wait failed.
+template <int QF, int NT, int UMAX, bool GB, class SH>
+__device__ bool gemm_tiles(const SmallParams& p, const SH& S, const SmallGemm& g, int t0, int nt, uint32_t seq0,
+                           const __half* xs, const __half* xg, int ldg, const EpiParams& ep, float rc, float rs) {
+  const int w = threadIdx.x >> 5, lane = threadIdx.x & 31, gi = lane >> 2, ti = lane & 3;
+  const int npg = pages_of(g);
+  int u0, u1;
+  r16::warp_units(g.K, w, &u0, &u1);
+  // B fragments from global memory first: their latency overlaps the page waits.
+  uint4 bq[GB ? UMAX : 1][NT];
+  if constexpr (GB) {
+#pragma unroll
+    for (int i = 0; i < UMAX; i++)
+#pragma unroll
+      for (int n = 0; n < NT; n++) {
+        const int u = u0 + i, m = 8 * n + gi;
+        const int k = (u >> 1) * TILE_K + 16 * ti + 8 * (u & 1);
+        bq[i][n] = (u < u1 && m < p.T) ? __ldcg(reinterpret_cast<const uint4*>(xg + (long)m * ldg + k))
+                                       : make_uint4(0, 0, 0, 0);
+      }
+  }
+  bool ok = true;
+  const int pg0 = (u0 >> 1) / PAGE_CHUNKS, pg1 = ((u1 - 1) >> 1) / PAGE_CHUNKS;
+  for (int i = 0; i < nt && ok; i++)
+    for (int pg = pg0; pg <= pg1 && ok; pg++) {
+      const uint32_t sq = seq0 + i * npg + pg;
+      ok = mbar_wait(S.bar0 + 8 * (sq % S.R), (sq / S.R) & 1, S.abort, p.status, 60);
+    }
+  float acc[MAX_TILES][NT][4];
+#pragma unroll
+  for (int i = 0; i < MAX_TILES; i++)
+#pragma unroll
+    for (int n = 0; n < NT; n++) acc[i][n][0] = acc[i][n][1] = acc[i][n][2] = acc[i][n][3] = 0.f;
+  if (ok) {
+#pragma unroll
+    for (int i = 0; i < UMAX; i++) {
+      const int u = u0 + i;
+      if (u >= u1) break;
+      const int c = u >> 1, hf = u & 1;
+      const int k = c * TILE_K + 16 * ti + 8 * hf;
+      uint4 b[NT];
+#pragma unroll
+      for (int n = 0; n < NT; n++)
+        b[n] = GB ? bq[GB ? i : 0][n] : *reinterpret_cast<const uint4*>(xs + (8 * n + gi) * LDX + k);
+#pragma unroll
+      for (int tt = 0; tt < MAX_TILES; tt++) {
+        if (tt >= nt) break;
+        const uint32_t sq = seq0 + tt * npg + c / PAGE_CHUNKS;
+        const uint8_t* chunk = S.ring + (sq % S.R) * SLOT + (c % PAGE_CHUNKS) * r16::chunk_bytes(QF);
+        const uint2 qa = *reinterpret_cast<const uint2*>(chunk + gi * TILE_K + 16 * ti + 8 * hf);
+        const uint2 qb = *reinterpret_cast<const uint2*>(chunk + (gi + 8) * TILE_K + 16 * ti + 8 * hf);
+        const uint4 ha = dq8_f16<QF>(qa, chunk + r16::CHUNK_Q, gi, 2 * ti + hf);
+        const uint4 hb = dq8_f16<QF>(qb, chunk + r16::CHUNK_Q, gi + 8, 2 * ti + hf);
+#pragma unroll
+        for (int n = 0; n < NT; n++) {
+          r16::mma16816(acc[tt][n], ha.x, hb.x, ha.y, hb.y, b[n].x, b[n].y);
+          r16::mma16816(acc[tt][n], ha.z, hb.z, ha.w, hb.w, b[n].z, b[n].w);
+        }
+      }
+    }
+  }
+#pragma unroll
+  for (int tt = 0; tt < MAX_TILES; tt++)
+    if (tt < nt) r16::store_partials<NT>(S.red + tt * NCW * NT * 32, acc[tt]);
+  bar_compute();
+  // The tiles' pages are free again: one arrival per warp on each.
+  if (lane == 0)
+    for (int q = 0; q < nt * npg; q++) mbar_arrive(S.bar0 + 8 * (S.R + (seq0 + q) % S.R));
+  if (*S.abort) return false;
+  for (int i = threadIdx.x; i < 64 * NT * nt; i += NCT) {
+    const int tt = i / (64 * NT), it = i % (64 * NT);
+    int q, m;
+    float va, vb;
+    r16::reduce_item<NT>(S.red + tt * NCW * NT * 32, it, &q, &m, &va, &vb);
+    if (m >= p.T) continue;
+    const int a = r16::pair_virtual_row(g.mode, t0 + tt, q);
+    if (ep.mode == EPI_QKV && a < ep.rope_cols) {
+      // epi_pair's RoPE with the preloaded table values.
+      const float x0 = __fsub_rn(__fmul_rn(va, rc), __fmul_rn(vb, rs));
+      const float x1 = __fadd_rn(__fmul_rn(va, rs), __fmul_rn(vb, rc));
+      *reinterpret_cast<uint32_t*>(ep.out16 + (long)m * ep.ldo + a) = pack_half2(x0, x1);
+    } else {
+      epi_pair(ep, m, a, va, vb);
+    }
+  }
+  bar_compute();  // the partials buffer is free for the next tiles
+  return true;
+}
+
+template <int NT, int UMAX, bool GB, class SH>
+__device__ bool gemm_tiles_any(const SmallParams& p, const SH& S, const SmallGemm& g, int t0, int nt,
+                               uint32_t seq0, const __half* xs, const __half* xg, int ldg, const EpiParams& ep,
+                               float rc = 0.f, float rs = 0.f) {
+  switch (g.qf) {
+    case QF_Q8_0: return gemm_tiles<QF_Q8_0, NT, UMAX, GB, SH>(p, S, g, t0, nt, seq0, xs, xg, ldg, ep, rc, rs);
+    case QF_KMIN: return gemm_tiles<QF_KMIN, NT, UMAX, GB, SH>(p, S, g, t0, nt, seq0, xs, xg, ldg, ep, rc, rs);
+    default: return gemm_tiles<QF_Q6K, NT, UMAX, GB, SH>(p, S, g, t0, nt, seq0, xs, xg, ldg, ep, rc, rs);
+  }
+}
+
+// The producer: every page of this CTA's share of every step, in the order
+// the compute warps consume them, into the ring (TMA bulk copies).
+template <class SH>
+__device__ void producer(const SmallParams& p, const SH& S) {
+  if ((threadIdx.x & 31) != 0) return;
+  uint32_t seq = 0;
+  bool ok = true;
+  for (int l = 0; l < p.n_layers && ok; l++) {
+    for (int m = 0; m < 4 && ok; m++) {
+      const SmallGemm& g = p.layers[l].g[m];
+      int t0, t1;
+      tile_range(m, g.tiles, &t0, &t1);
+      const uint32_t bytes = PAGE_CHUNKS * r16::chunk_bytes(g.qf);
+      for (int t = t0; t < t1 && ok; t++) {
+        for (int pg = 0; pg < pages_of(g) && ok; pg++, seq++) {
+          const uint32_t slot = seq % S.R, use = seq / S.R;
+          if (use > 0) ok = mbar_wait(S.bar0 + 8 * (S.R + slot), (use - 1) & 1, S.abort, p.status, 61);
+          if (!ok) break;
+          const uint8_t* src = g.w + (long)t * (g.K / TILE_K) * r16::chunk_bytes(g.qf) + (long)pg * bytes;
+          mbar_expect_tx(S.bar0 + 8 * slot, bytes);
+          bulk_load(tcx::smem_u32(S.ring + slot * SLOT), src, bytes, S.bar0 + 8 * slot);
+        }
+      }
+    }
+  }
+  // Copies still in flight (after a failure) must land before the CTA exits.
+  const uint32_t first = seq > (uint32_t)S.R ? seq - S.R : 0;
+  volatile int no_abort = 0;
+  for (uint32_t sq = first; sq < seq; sq++)
+    mbar_wait(S.bar0 + 8 * (sq % S.R), (sq / S.R) & 1, &no_abort, nullptr, 62);
+}
+
+template <int NT>
 __global__ void __launch_bounds__(NTHREADS, 1) forward_small_kernel(const __grid_constant__ SmallParams p) {
-  extern __shared__ __align__(16) uint8_t smem[];
-  const uint32_t sbase = (uint32_t)__cvta_generic_to_shared(smem);
-  float* h = reinterpret_cast<float*>(smem + SmemLayout::OFF_H);
-  uint8_t* U = smem + SmemLayout::OFF_U;
-  __half* x = reinterpret_cast<__half*>(U);
-  const uint32_t u_addr = sbase + SmemLayout::OFF_U;
-  int* flag = reinterpret_cast<int*>(smem + SmemLayout::OFF_MISC);
+  using L = Lay<NT>;
+  extern __shared__ __align__(128) uint8_t smem[];
+  SharedT<L::R> S;
+  S.ring = smem + L::OFF_RING;
+  S.h = reinterpret_cast<float*>(smem + L::OFF_H);
+  S.U = smem + L::OFF_U;
+  S.x = reinterpret_cast<__half*>(S.U);
+  S.red = reinterpret_cast<float4*>(smem + L::OFF_RED);
+  S.bar0 = tcx::smem_u32(smem + L::OFF_BAR);
+  S.abort = reinterpret_cast<volatile int*>(smem + L::OFF_MISC);
+  S.flag = reinterpret_cast<volatile int*>(smem + L::OFF_MISC + 4);
   const int T = p.T;
 
-  // Token positions inside their sequences (offsets[nseq+1], packed; empty
-  // sequences are skipped).  Every CTA writes the same values.
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < L::R; i++) {
+      mbar_init(S.bar0 + 8 * i, 1);
+      mbar_init(S.bar0 + 8 * (L::R + i), NCW);
+    }
+    *S.abort = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  __syncthreads();
+  if (threadIdx.x >= NCT) {
+    producer(p, S);
+    return;
+  }
+
+  // Token positions inside their sequences (every CTA writes the same values).
+  prefetch_small(p);
   if (threadIdx.x < T) {
     const int t = threadIdx.x;
     int s = 0;
     while (s + 1 < p.nseq && p.offsets[s + 1] <= t) s++;
     p.pos[t] = t - p.offsets[s];
   }
-  // Weight step w = 4 * layer + m (m: 0 qkv, 1 out, 2 upgate, 3 down).
-  const int nsteps = 4 * p.n_layers;
-  prefetch_slice(p.layers[0].g[0], sbase + SmemLayout::OFF_W);
-  cp_async_commit();
-  embed_rows(p, h, T);
-  __syncthreads();
-  ln_rows(h, x, nullptr, p.embd_w, p.embd_b, p.eps, T);
+  embed_rows(p, S.h, S.U, T);
+  bar_compute();
+  ln_rows(S.h, S.x, nullptr, p.embd_w, p.embd_b, p.eps, T);
+  bar_compute();
 
-  unsigned bar = 0;
-  for (int w = 0; w < nsteps; w++) {
-    const int l = w >> 2, m = w & 3;
-    const SmallLayer& L = p.layers[l];
-    const SmallGemm& g = L.g[m];
-    // This step's input, if other CTAs produced it (one group), then the
-    // next step's weight slice into the other buffer (the newest group);
-    // wait for everything but the newest.
-    if (m == 1) stage_rows(u_addr, p.att, T, H);
-    if (m == 3) stage_rows(u_addr, p.ff, T, F);
-    cp_async_commit();
-    if (w + 1 < nsteps)
-      prefetch_slice(p.layers[(w + 1) >> 2].g[(w + 1) & 3], sbase + SmemLayout::OFF_W + ((w + 1) & 1) * WBUF_BYTES);
-    cp_async_commit();
-    cp_async_wait1();
-    __syncthreads();
-    const uint8_t* wbuf = smem + SmemLayout::OFF_W + (w & 1) * WBUF_BYTES;
-    EpiParams ep{};
-    ep.M = T;
-    if (m == 0) {
-      // Residual LayerNorm after the previous layer's FFN (the embedding
-      // LayerNorm for layer 0 ran above), then QKV with RoPE.
-      if (l > 0) ln_rows(h, x, p.y, p.layers[l - 1].out_w, p.layers[l - 1].out_b, p.eps, T);
-      __syncthreads();
+  uint32_t seq = 0;  // next page of this CTA's sequence
+  const int G = gridDim.x;
+  for (int l = 0; l < p.n_layers; l++) {
+    const SmallLayer& Ly = p.layers[l];
+    // ---- QKV: residual LayerNorm of the previous layer's FFN, QKV + RoPE.
+    {
+      const SmallGemm& g = Ly.g[0];
+      int t0, t1;
+      tile_range(0, g.tiles, &t0, &t1);
+      // The RoPE table values of this thread's first-tile output item, loaded
+      // before the wait.
+      float rc = 0.f, rs = 0.f;
+      if (t1 > t0 && threadIdx.x < 64 * NT) {
+        int q, m;
+        q = (threadIdx.x & 63) >> 3;
+        m = 8 * (threadIdx.x >> 6) + 2 * ((threadIdx.x >> 1) & 3) + (threadIdx.x & 1);
+        const int a = 16 * t0 + 2 * q;
+        if (m < T && a < 2 * H) {
+          const long r = (long)p.pos[m] * (HD / 2) + ((a % HD) >> 1);
+          rc = __ldg(p.rope_cos + r);
+          rs = __ldg(p.rope_sin + r);
+        }
+      }
+      if (l > 0) {
+        if (!wait_cnt(p, S, CNT_Y2, (unsigned)(p.layers[0].g[3].tiles * l), 70)) return;
+        ln_rows(S.h, S.x, p.y2, p.layers[l - 1].out_w, p.layers[l - 1].out_b, p.eps, T);
+        bar_compute();
+      }
+      EpiParams ep{};
+      ep.M = T;
       ep.mode = EPI_QKV;
       ep.N = 3 * H;
       ep.out16 = p.qkv;
@@ -394,41 +513,90 @@ __global__ void __launch_bounds__(NTHREADS, 1) forward_small_kernel(const __grid
       ep.rope_sin = p.rope_sin;
       ep.head_dim = HD;
       ep.rope_cols = 2 * H;
-      gemm_any(g, wbuf, x, T, ep);
-      if (!grid_sync(p.barrier, bar++, p.status, flag)) return;
-      attention_step(p, U);  // U (x) is free again
-      if (!grid_sync(p.barrier, bar++, p.status, flag)) return;
-    } else if (m == 1) {
+      for (int t = t0; t < t1; t++) {
+        // RoPE values preloaded for the first tile only.
+        const bool pre = t == t0;
+        if (pre) {
+          if (!gemm_tiles_any<NT, 3, false>(p, S, g, t, 1, seq, S.x, nullptr, 0, ep, rc, rs)) return;
+        } else {
+          if (!gemm_tiles_any<NT, 3, false>(p, S, g, t, 1, seq, S.x, nullptr, 0, ep, 0.f, 0.f)) return;
+        }
+        seq += pages_of(g);
+        signal(p, CNT_QKV + ((16 * t) % H) / HD);
+      }
+    }
+    // ---- Attention of one head, once its 12 QKV tiles are in.
+    for (int hd = 0; hd < HEADS; hd++) {
+      if (att_cta(hd) != (int)blockIdx.x) continue;
+      if (!wait_cnt(p, S, CNT_QKV + hd, (unsigned)(3 * HD / 16 * (l + 1)), 71)) return;
+      attention_head(p, S.U, hd);
+      signal(p, CNT_ATT);
+    }
+    // ---- Output projection tiles, once every head is in.
+    {
+      const SmallGemm& g = Ly.g[1];
+      int t0, t1;
+      tile_range(1, g.tiles, &t0, &t1);
+      if (t1 > t0 && !wait_cnt(p, S, CNT_ATT, (unsigned)(HEADS * (l + 1)), 72)) return;
+      EpiParams ep{};
+      ep.M = T;
       ep.mode = EPI_F32;
       ep.N = H;
-      ep.out32 = p.y;
+      ep.out32 = p.y1;
       ep.ldo = H;
-      gemm_any(g, wbuf, x, T, ep);  // x = staged attention output
-      if (!grid_sync(p.barrier, bar++, p.status, flag)) return;
-    } else if (m == 2) {
-      ln_rows(h, x, p.y, L.attn_w, L.attn_b, p.eps, T);
-      __syncthreads();
+      for (int t = t0; t < t1; t++) {
+        if (!gemm_tiles_any<NT, 3, true>(p, S, g, t, 1, seq, nullptr, p.att, H, ep)) return;
+        seq += pages_of(g);
+        signal(p, CNT_Y1);
+      }
+    }
+    // ---- Up/gate: residual LayerNorm after attention, GEGLU tiles.
+    {
+      if (!wait_cnt(p, S, CNT_Y1, (unsigned)(Ly.g[1].tiles * (l + 1)), 73)) return;
+      ln_rows(S.h, S.x, p.y1, Ly.attn_w, Ly.attn_b, p.eps, T);
+      bar_compute();
+      EpiParams ep{};
+      ep.M = T;
       ep.mode = EPI_GEGLU;
       ep.N = F;
       ep.out16 = p.ff;
       ep.ldo = F;
-      gemm_any(g, wbuf, x, T, ep);
-      if (!grid_sync(p.barrier, bar++, p.status, flag)) return;
-    } else {
+      const SmallGemm& g = Ly.g[2];
+      int t0, t1;
+      tile_range(2, g.tiles, &t0, &t1);
+      for (int t = t0; t < t1; t += MAX_TILES) {
+        const int n = t1 - t < MAX_TILES ? t1 - t : MAX_TILES;
+        if (!gemm_tiles_any<NT, 3, false>(p, S, g, t, n, seq, S.x, nullptr, 0, ep)) return;
+        seq += n * pages_of(g);
+      }
+      signal(p, CNT_FF);
+    }
+    // ---- Down projection tiles, once every CTA finished up/gate.
+    {
+      const SmallGemm& g = Ly.g[3];
+      int t0, t1;
+      tile_range(3, g.tiles, &t0, &t1);
+      if (t1 > t0 && !wait_cnt(p, S, CNT_FF, (unsigned)(G * (l + 1)), 74)) return;
+      EpiParams ep{};
+      ep.M = T;
       ep.mode = EPI_F32;
       ep.N = H;
-      ep.out32 = p.y;
+      ep.out32 = p.y2;
       ep.ldo = H;
-      gemm_any(g, wbuf, x, T, ep);  // x = staged GEGLU output [T][F]
-      if (!grid_sync(p.barrier, bar++, p.status, flag)) return;
+      for (int t = t0; t < t1; t++) {
+        if (!gemm_tiles_any<NT, 12, true>(p, S, g, t, 1, seq, nullptr, p.ff, F, ep)) return;
+        seq += pages_of(g);
+        signal(p, CNT_Y2);
+      }
     }
   }
-  asm volatile("cp.async.wait_all;" ::: "memory");
   // Final residual LayerNorm; one CTA writes h for the pooling kernel.
   if (blockIdx.x == 0) {
-    ln_rows(h, x, p.y, p.layers[p.n_layers - 1].out_w, p.layers[p.n_layers - 1].out_b, p.eps, T);
-    __syncthreads();
-    for (int i = threadIdx.x; i < T * H; i += NTHREADS) p.h_out[i] = h[i];
+    const SmallLayer& last = p.layers[p.n_layers - 1];
+    if (!wait_cnt(p, S, CNT_Y2, (unsigned)(last.g[3].tiles * p.n_layers), 75)) return;
+    ln_rows(S.h, S.x, p.y2, last.out_w, last.out_b, p.eps, T);
+    bar_compute();
+    for (int i = threadIdx.x; i < T * H; i += NCT) p.h_out[i] = S.h[i];
   }
 }
 
@@ -436,17 +604,19 @@ __global__ void __launch_bounds__(NTHREADS, 1) forward_small_kernel(const __grid
 
 bool small_forward_supported(const SmallParams& p, int hidden, int ffn, int heads, int sms) {
   if (hidden != SMALL_HIDDEN || ffn != SMALL_FFN || heads != SMALL_HEADS || p.T < 1 || p.T > SMALL_MAX_TOKENS ||
-      p.n_layers < 1 || p.n_layers > SMALL_MAX_LAYERS || sms < 1)
+      p.n_layers < 1 || p.n_layers > SMALL_MAX_LAYERS || sms < fs::HEADS)
     return false;
-  // Every step's slice must fit a weight buffer with one CTA per SM.
   for (int l = 0; l < p.n_layers; l++)
-    for (const SmallGemm& g : p.layers[l].g) {
-      if (!g.w || g.K % TILE_K || g.K > 32 * 16 * 8) return false;
-      const long pairs = (g.n_pairs + sms - 1) / sms;
-      if (pairs * (g.K / TILE_K) * 2 * (64 + fs::meta_row_bytes(g.qf)) > fs::WBUF_BYTES) return false;
+    for (int m = 0; m < 4; m++) {
+      const SmallGemm& g = p.layers[l].g[m];
+      if (!g.w || g.K % fs::PAGE_COLS || (g.qf != QF_Q8_0 && g.qf != QF_KMIN && g.qf != QF_Q6K)) return false;
+      const int want = m == 0 ? 3 * SMALL_HIDDEN / 16 : m == 2 ? SMALL_FFN / 8 : SMALL_HIDDEN / 16;
+      if (g.tiles != want) return false;
     }
   return true;
 }
+
+size_t small_sync_bytes() { return (size_t)fs::N_CNT * fs::CNT_STRIDE * 4; }
 
 cudaError_t launch_forward_small(const SmallParams& p, cudaStream_t s) {
   static std::mutex mu;
@@ -454,34 +624,42 @@ cudaError_t launch_forward_small(const SmallParams& p, cudaStream_t s) {
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev >= 64) return cudaErrorInvalidDevice;
+  const bool two = p.T > 8;
   {
     std::lock_guard<std::mutex> lk(mu);
     if (grid[dev] == 0) {
-      cudaError_t e = cudaFuncSetAttribute(fs::forward_small_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                           fs::SmemLayout::BYTES);
+      cudaError_t e = cudaFuncSetAttribute(fs::forward_small_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                           fs::Lay<1>::BYTES);
+      if (e == cudaSuccess)
+        e = cudaFuncSetAttribute(fs::forward_small_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 fs::Lay<2>::BYTES);
       if (e != cudaSuccess) return e;
-      int sms = 0, per_sm = 0;
+      int sms = 0, per_sm1 = 0, per_sm2 = 0;
       cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-      e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, fs::forward_small_kernel, fs::NTHREADS,
-                                                        fs::SmemLayout::BYTES);
+      e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm1, fs::forward_small_kernel<1>, fs::NTHREADS,
+                                                        fs::Lay<1>::BYTES);
+      if (e == cudaSuccess)
+        e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm2, fs::forward_small_kernel<2>, fs::NTHREADS,
+                                                          fs::Lay<2>::BYTES);
       if (e != cudaSuccess) return e;
-      if (per_sm < 1) return cudaErrorNotSupported;
+      if (per_sm1 < 1 || per_sm2 < 1) return cudaErrorNotSupported;
       grid[dev] = sms;  // one CTA per SM
     }
   }
-  cudaError_t e = cudaMemsetAsync(p.barrier, 0, sizeof(unsigned), s);
+  cudaError_t e = cudaMemsetAsync(p.sync, 0, small_sync_bytes(), s);
   if (e != cudaSuccess) return e;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(grid[dev]);
   cfg.blockDim = dim3(fs::NTHREADS);
-  cfg.dynamicSmemBytes = fs::SmemLayout::BYTES;
+  cfg.dynamicSmemBytes = two ? fs::Lay<2>::BYTES : fs::Lay<1>::BYTES;
   cfg.stream = s;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeCooperative;
   attr[0].val.cooperative = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, fs::forward_small_kernel, p);
+  return two ? cudaLaunchKernelEx(&cfg, fs::forward_small_kernel<2>, p)
+             : cudaLaunchKernelEx(&cfg, fs::forward_small_kernel<1>, p);
 }
 
 }  // namespace le

@@ -15,6 +15,8 @@ cudaError_t launch_repack(int type, const uint8_t* src0, const uint8_t* src1, lo
 cudaError_t launch_dequant_tiles(int qf, const uint8_t* w, int n_rows, int K, int mode, float* out, cudaStream_t s);
 cudaError_t launch_gguf_rows(int type, const uint8_t* src, long row_bytes, int n_rows, int K, float* out, cudaStream_t s);
 cudaError_t launch_expand_f16(int qf, const uint8_t* w, int n_rows, int K, __half* out, cudaStream_t s);
+cudaError_t launch_repack_r16(int qf, const uint8_t* t128, int K, int geglu, int tiles, uint8_t* out,
+                              cudaStream_t s);
 cudaError_t launch_f32_rows_to_f16(const float* src0, const float* src1, int N_src, int K, int n_virt, int interleave,
                                    __half* out, cudaStream_t s);
 
@@ -41,16 +43,16 @@ cudaError_t launch_attention_stc(const __half* qkv, const int32_t* offsets, int 
 cudaError_t launch_attention_tc(const __half* qkv, const int32_t* offsets, int nseq, int T, int max_len, int min_len,
                                 int H, int heads, __half* out, DevStatus* status, cudaStream_t s);
 
-// gemm_simt.cu
-cudaError_t launch_gemm_simt(int qf, const uint8_t* W, int n_virtual, int K, const __half* A, long lda,
-                             const EpiParams& ep, cudaStream_t s);
+// gemm_r16.cu: fewer than 64 tokens (row16 weight layout, gemm_r16.cuh)
+cudaError_t launch_gemm_r16(int qf, const uint8_t* W, int n_tiles, int K, const __half* A, long lda,
+                            const EpiParams& ep, cudaStream_t s);
 
 // gemm_tc2.cu
 cudaError_t launch_gemm_tc2(int qf, const uint8_t* W, int n_virtual, int K, const __half* A, long lda,
                             const EpiParams& ep, DevStatus* status, cudaStream_t s);
 
 // forward_small.cu: the whole forward for at most SMALL_MAX_TOKENS tokens in
-// one cooperative kernel (nomic-bert shape only).
+// one cooperative kernel (nomic-bert shape, quantised weights only).
 constexpr int SMALL_HIDDEN = 768;
 constexpr int SMALL_FFN = 3072;
 constexpr int SMALL_HEADS = 12;
@@ -58,10 +60,10 @@ constexpr int SMALL_MAX_TOKENS = 16;
 constexpr int SMALL_MAX_LAYERS = 24;
 
 struct SmallGemm {
-  const uint8_t* w;  // tile-blocked quantised weight
+  const uint8_t* w;  // row16 layout of the weight (gemm_r16.cuh)
   int qf;            // its QFmt
   int K;
-  int n_pairs;       // output row pairs (epilogue.cuh pair_rows)
+  int tiles;         // row16 tiles
   int mode;          // EpiMode of the step
 };
 struct SmallLayer {
@@ -82,14 +84,16 @@ struct SmallParams {
   int32_t* pos;   // [T] positions (written)
   __half* qkv;    // [T][3H]
   __half* att;    // [T][H]
-  float* y;       // [T][H]
+  float* y1;      // [T][H] attention-output projection
   __half* ff;     // [T][F]
+  float* y2;      // [T][H] down projection
   float* h_out;   // [T][H] final hidden states
-  unsigned* barrier;
+  unsigned* sync; // small_sync_bytes() of hand-off counters, zeroed by the launch
   DevStatus* status;
   SmallLayer layers[SMALL_MAX_LAYERS];
 };
 bool small_forward_supported(const SmallParams& p, int hidden, int ffn, int heads, int sms);
+size_t small_sync_bytes();
 cudaError_t launch_forward_small(const SmallParams& p, cudaStream_t s);
 
 // gemm_ln.cu: projection to 768 columns with the residual add and

@@ -1,6 +1,7 @@
 // Weight upload support: GGUF block decode, repack into the tile-blocked
 // layout (common.cuh), and exact dequantisation back to [N][K] float32.
 #include "dequant.cuh"
+#include "gemm_r16.cuh"
 #include "gguf_decode.cuh"
 #include "kernels.h"
 
@@ -149,6 +150,45 @@ __global__ void f32_rows_to_f16_kernel(const float* __restrict__ src0, const flo
   *reinterpret_cast<uint4*>(out + (long)v * K + c) = h;
 }
 
+// The row16 layout (gemm_r16.cuh) from the 128-row tile layout: one thread
+// per (tile, 64-column chunk, row) copies the row's 64 quant bytes and its
+// metadata.  Tile j row r takes virtual row v: for the merged up/gate matrix
+// (geglu) up[8j + r] (r < 8) or gate[8j + r - 8] in the 128-row tiles' order
+// (64 up rows then 64 gate rows per tile), otherwise feature 16j + 2r
+// (r < 8) or 16j + 2(r - 8) + 1.
+template <int QF>
+__global__ void repack_r16_kernel(const uint8_t* __restrict__ t128, int K, int geglu, int tiles,
+                                  uint8_t* __restrict__ out) {
+  const int ksteps = K / TILE_K;
+  const long idx = (long)blockIdx.x * blockDim.x + threadIdx.x;
+  if (idx >= (long)tiles * ksteps * r16::ROWS) return;
+  const int r = (int)(idx % r16::ROWS);
+  const int c = (int)((idx / r16::ROWS) % ksteps);
+  const int j = (int)(idx / r16::ROWS / ksteps);
+  int v;
+  if (geglu) {
+    const int f = 8 * j + (r & 7);
+    v = (f / (TILE_N / 2)) * TILE_N + (r < 8 ? 0 : TILE_N / 2) + f % (TILE_N / 2);
+  } else {
+    v = 16 * j + (r < 8 ? 2 * r : 2 * (r - 8) + 1);
+  }
+  constexpr int MRB = r16::meta_row_bytes(QF);
+  const uint8_t* src = t128 + ((long)(v / TILE_N) * ksteps + c) * chunk_bytes(QF);
+  const int sr = v % TILE_N;
+  uint8_t* dst = out + ((long)j * ksteps + c) * r16::chunk_bytes(QF);
+  const uint4* q = reinterpret_cast<const uint4*>(src + sr * TILE_K);
+  uint4* d = reinterpret_cast<uint4*>(dst + r * TILE_K);
+#pragma unroll
+  for (int i = 0; i < 4; i++) d[i] = q[i];
+  const uint8_t* ms = src + TILE_Q_BYTES + sr * MRB;
+  uint8_t* md = dst + r16::CHUNK_Q + r * MRB;
+  if constexpr (MRB == 16) {
+    *reinterpret_cast<uint4*>(md) = *reinterpret_cast<const uint4*>(ms);
+  } else {
+    *reinterpret_cast<uint32_t*>(md) = *reinterpret_cast<const uint32_t*>(ms);
+  }
+}
+
 // Dequantise whole GGUF rows (used for the embedding table check).
 __global__ void gguf_rows_kernel(int type, const uint8_t* __restrict__ src, long row_bytes, int n_rows, int K,
                                  float* __restrict__ out) {
@@ -190,6 +230,19 @@ cudaError_t launch_dequant_tiles(int qf, const uint8_t* w, int n_rows, int K, in
 cudaError_t launch_gguf_rows(int type, const uint8_t* src, long row_bytes, int n_rows, int K, float* out, cudaStream_t s) {
   const long n = (long)n_rows * K;
   gguf_rows_kernel<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(type, src, row_bytes, n_rows, K, out);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_repack_r16(int qf, const uint8_t* t128, int K, int geglu, int tiles, uint8_t* out,
+                              cudaStream_t s) {
+  const long n = (long)tiles * (K / TILE_K) * r16::ROWS;
+  const unsigned grid = (unsigned)((n + 255) / 256);
+  switch (qf) {
+    case QF_Q8_0: repack_r16_kernel<QF_Q8_0><<<grid, 256, 0, s>>>(t128, K, geglu, tiles, out); break;
+    case QF_KMIN: repack_r16_kernel<QF_KMIN><<<grid, 256, 0, s>>>(t128, K, geglu, tiles, out); break;
+    case QF_Q6K: repack_r16_kernel<QF_Q6K><<<grid, 256, 0, s>>>(t128, K, geglu, tiles, out); break;
+    default: return cudaErrorInvalidValue;
+  }
   return cudaGetLastError();
 }
 
