@@ -193,6 +193,35 @@ typedef struct {
 int le_set_profiling(le_model* m, int enable);
 int le_get_stats(le_model* m, le_stats* out, int reset);
 
+/* Host tokenizer: internal/embed/tokenizer.go (WordPieceTokenizer,
+ * LoadTokenizer, Encode) in C++, for hosts that hand texts to the library.
+ * Token ids follow the reference's rules exactly: Go's strings.ToLower,
+ * split on unicode.IsSpace and BERT punctuation, greedy longest match over
+ * each word's UTF-8 bytes with the U+2581 prefix on the first piece, byte and
+ * [UNK]=100 fallbacks, [CLS]=101 ... [SEP]=102, truncation keeping [SEP].
+ * A tokenizer is read-only after creation: any number of threads may call
+ * le_tokenize on it concurrently. */
+typedef struct le_tokenizer le_tokenizer;
+/* Vocabulary: token i (token_lens[i] bytes) has id i; a later duplicate wins
+ * (tokenizer.go:29-35). */
+int le_tokenizer_create(const char* const* tokens, const int32_t* token_lens, int n_tokens, le_tokenizer** out);
+/* The vocabulary of a GGUF file's "tokenizer.ggml.tokens" string array
+ * (tokenizer.go:24-44, readGGUFStringArray). */
+int le_tokenizer_load_gguf(const char* path, le_tokenizer** out);
+int le_tokenizer_vocab_size(const le_tokenizer* t, int* n);
+int le_tokenizer_free(le_tokenizer* t);
+/* Encode texts packed back to back in `text` (text i = bytes
+ * text[text_offsets[i] .. text_offsets[i+1]), UTF-8; invalid bytes read as
+ * U+FFFD as Go does) with `prefix` (NUL-terminated, may be NULL) prepended
+ * (embedder.go:48-51), truncated to max_len ids (>= 2).  Writes offsets
+ * [n_texts+1] and the packed ids (text i = ids[offsets[i] .. offsets[i+1])),
+ * ready for le_embed_ids; if capacity (in ids) is too small, returns
+ * LE_EINVAL with the offsets filled in, so offsets[n_texts] is the size to
+ * allocate.  n_texts * max_len is always enough.  nthreads <= 0: all
+ * hardware threads. */
+int le_tokenize(const le_tokenizer* t, const char* text, const int64_t* text_offsets, int n_texts, const char* prefix,
+                int max_len, int32_t* ids, int64_t capacity, int32_t* offsets, int nthreads);
+
 /* Library / device description for health endpoints (sgemm.go:263
  * SgemmInfo): device count, SM count, kernel variants, precision mode. */
 int le_info(char* buf, int len);

@@ -42,7 +42,7 @@ def _host_compiler() -> list[str]:
 
 def build(verbose: bool = False, force: bool = False) -> str:
     os.makedirs(OBJ, exist_ok=True)
-    srcs = sorted(glob.glob(os.path.join(CSRC, "*.cu")))
+    srcs = sorted(glob.glob(os.path.join(CSRC, "*.cu")) + glob.glob(os.path.join(CSRC, "*.cpp")))
     headers = glob.glob(os.path.join(CSRC, "*.cuh")) + glob.glob(os.path.join(CSRC, "*.h")) + \
         glob.glob(os.path.join(HERE, "..", "include", "*.h"))
     newest_hdr = max((os.path.getmtime(h) for h in headers), default=0)
@@ -50,7 +50,7 @@ def build(verbose: bool = False, force: bool = False) -> str:
     hc = _host_compiler()
 
     def compile_one(src: str) -> str:
-        obj = os.path.join(OBJ, os.path.basename(src)[:-3] + ".o")
+        obj = os.path.join(OBJ, os.path.splitext(os.path.basename(src))[0] + ".o")
         if not force and os.path.exists(obj) and os.path.getmtime(obj) >= max(os.path.getmtime(src), newest_hdr):
             return obj
         cmd = [nvcc, *hc, *NVFLAGS, "-c", src, "-o", obj]

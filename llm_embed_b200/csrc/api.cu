@@ -38,6 +38,17 @@ static int fail(int code, const char* fmt, ...) {
   return code;
 }
 
+// The same for the library's other host sources (tokenizer.cpp).
+int le_fail(int code, const char* fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof buf, fmt, ap);
+  va_end(ap);
+  g_err = buf;
+  return code;
+}
+
 #define CK(call)                                                                                 \
   do {                                                                                           \
     cudaError_t e_ = (call);                                                                     \

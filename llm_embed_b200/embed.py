@@ -12,12 +12,10 @@ from __future__ import annotations
 
 import ctypes as C
 import os
-import struct
 import threading
 
 import numpy as np
 
-from .tokenizer import WordPieceTokenizer
 
 _HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(_HERE, "libllmembed_cuda.so")
@@ -91,6 +89,12 @@ def lib() -> C.CDLL:
             L.le_qgemm_device_noalloc.argtypes = [vp, vp, C.c_int, vp, vp]
             L.le_qweight_free.argtypes = [vp]
             L.le_qweight_sync.argtypes = [vp]
+            L.le_tokenizer_create.argtypes = [C.POINTER(C.c_char_p), ip, C.c_int, C.POINTER(vp)]
+            L.le_tokenizer_load_gguf.argtypes = [C.c_char_p, C.POINTER(vp)]
+            L.le_tokenizer_vocab_size.argtypes = [vp, C.POINTER(C.c_int)]
+            L.le_tokenizer_free.argtypes = [vp]
+            L.le_tokenize.argtypes = [vp, C.c_char_p, C.POINTER(C.c_int64), C.c_int, C.c_char_p, C.c_int, ip,
+                                      C.c_int64, ip, C.c_int]
             L.le_info.argtypes = [C.c_char_p, C.c_int]
             L.le_set_profiling.argtypes = [vp, C.c_int]
             L.le_get_stats.argtypes = [vp, C.POINTER(Stats), C.c_int]
@@ -129,10 +133,78 @@ def pack(seqs) -> tuple[np.ndarray, np.ndarray]:
     return np.ascontiguousarray(ids, np.int32), offs
 
 
+class Tokenizer:
+    """The library's C++ host tokenizer (le_tokenizer_*): the rules of
+    internal/embed/tokenizer.go, multithreaded over a batch of texts.  Same
+    Encode/VocabSize interface as tokenizer.WordPieceTokenizer (its Python
+    restatement)."""
+
+    def __init__(self, handle):
+        self._h = handle
+
+    @classmethod
+    def Load(cls, path: str) -> "Tokenizer":
+        h = C.c_void_p()
+        _check(lib().le_tokenizer_load_gguf(path.encode(), C.byref(h)))
+        return cls(h.value)
+
+    @classmethod
+    def from_tokens(cls, tokens) -> "Tokenizer":
+        toks = [t if isinstance(t, bytes) else t.encode() for t in tokens]
+        arr = (C.c_char_p * len(toks))(*toks)
+        lens = np.array([len(t) for t in toks], np.int32)
+        h = C.c_void_p()
+        _check(lib().le_tokenizer_create(arr, _p(lens, C.c_int32), len(toks), C.byref(h)))
+        return cls(h.value)
+
+    def VocabSize(self) -> int:
+        n = C.c_int(0)
+        _check(lib().le_tokenizer_vocab_size(self._h, C.byref(n)))
+        return n.value
+
+    @staticmethod
+    def pack_texts(texts):
+        """Texts as one UTF-8 buffer and int64 offsets [n+1] (le_tokenize's input)."""
+        raw = [t if isinstance(t, bytes) else t.encode("utf-8", "surrogatepass") for t in texts]
+        toffs = np.zeros(len(raw) + 1, np.int64)
+        toffs[1:] = np.cumsum(np.fromiter(map(len, raw), np.int64, len(raw)))
+        return b"".join(raw), toffs
+
+    def encode_batch(self, texts, max_len: int, prefix: str = "", nthreads: int = 0):
+        """(ids int32, offsets int32 [n+1]) of prefix + text for each text."""
+        return self.encode_packed(*self.pack_texts(texts), max_len, prefix, nthreads)
+
+    def encode_packed(self, buf: bytes, toffs: np.ndarray, max_len: int, prefix: str = "", nthreads: int = 0):
+        """encode_batch on texts already packed by pack_texts."""
+        n = toffs.size - 1
+        offs = np.zeros(n + 1, np.int32)
+        ids = np.empty(max(n * max_len, 1), np.int32)
+        _check(lib().le_tokenize(self._h, buf, toffs.ctypes.data_as(C.POINTER(C.c_int64)), n,
+                                 prefix.encode("utf-8", "surrogatepass"), max_len, _p(ids, C.c_int32), ids.size,
+                                 _p(offs, C.c_int32), nthreads))
+        return ids[:offs[-1]].copy(), offs
+
+    def Encode(self, text, max_len: int) -> tuple[list[int], list[int]]:
+        """Encode (tokenizer.go:47-80): token ids and the all-ones mask."""
+        ids, _ = self.encode_batch([text], max_len)
+        return ids.tolist(), [1] * len(ids)
+
+    def close(self):
+        if self._h:
+            lib().le_tokenizer_free(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
 class Embedder:
     """One model replica per device; EmbedIDs shards sequences across them."""
 
-    def __init__(self, handles, hp: HParams, tokenizer: WordPieceTokenizer | None = None):
+    def __init__(self, handles, hp: HParams, tokenizer: "Tokenizer | None" = None):
         self._handles = (C.c_void_p * len(handles))(*handles)
         self._n = len(handles)
         self.hparams = hp
@@ -159,13 +231,14 @@ class Embedder:
         # The model file parsed, so its KV section is readable; a file without
         # tokenizer.ggml.tokens still embeds token ids.
         try:
-            tok = WordPieceTokenizer.Load(model_path)
-        except KeyError:
-            tok = None
-        except (OSError, ValueError, struct.error) as err:
-            for h in handles:
-                lib().le_model_free(h)
-            raise LlmEmbedError(LE_EIO, f"tokenizer: {err}") from err
+            tok = Tokenizer.Load(model_path)
+        except LlmEmbedError as err:
+            if "not found" in str(err):
+                tok = None
+            else:
+                for h in handles:
+                    lib().le_model_free(h)
+                raise
         return cls(handles, hp, tok)
 
     @classmethod
@@ -239,11 +312,15 @@ class Embedder:
         return self.EmbedIDs(i, o)[0]
 
     # embedder.go:75 EmbedBatch: texts (or id sequences), one device call for
-    # the whole batch instead of one forward per text.
+    # the whole batch instead of one forward per text; texts are tokenised
+    # together by the C++ tokenizer's threads.
     def EmbedBatch(self, texts) -> list[np.ndarray]:
         if len(texts) == 0:
             return []
-        i, o = pack([self._ids(t) for t in texts])
+        if self.tokenizer is not None and all(isinstance(t, str) for t in texts):
+            i, o = self.tokenizer.encode_batch(texts, self.hparams.context_length, prefix=self.TaskPrefix)
+        else:
+            i, o = pack([self._ids(t) for t in texts])
         return list(self.EmbedIDs(i, o))
 
     def embed_device(self, d_ids: int, d_offsets: int, nseq: int, n_tokens: int, max_len: int, d_out: int,

@@ -521,8 +521,8 @@ def test_large_batch_rows_match_mid_batch(model_path):
     LayerNorm fused into the GEMM (three CTA pairs per 256-row block, row
     statistics exchanged through global memory); 64..255 tokens run GEMM +
     separate LayerNorm.  Both reduce each row in the same order, so a
-    sequence's embedding is the same bits in either, including in a batch
-    whose last token tile is partial."""
+    sequence's embedding is the same bits in either, and in a batch of 939
+    or 7,033 tokens, including batches whose last token tile is partial."""
     spec = small_spec()
     e = Embedder.Load(model_path(spec))
     try:
@@ -533,6 +533,12 @@ def test_large_batch_rows_match_mid_batch(model_path):
         mid = e.EmbedIDs(ids[:offs[k]], offs[:k + 1])
         assert offs[k] >= 64 and offs[-1] >= 256 and offs[-1] % 128 != 0
         assert np.array_equal(big[:k].view(np.uint32), mid.view(np.uint32))
+        # The 939 tokens followed by more sequences, 7,033 tokens in all.
+        more = [101] * 61 + [35]
+        ids2, offs2 = synth.make_ids(lens + more, seed=11, vocab=spec.vocab)
+        assert np.array_equal(ids2[:offs[-1]], ids) and offs2[-1] >= 7000
+        huge = e.EmbedIDs(ids2, offs2)
+        assert np.array_equal(huge[:len(lens)].view(np.uint32), big.view(np.uint32))
     finally:
         e.Close()
     ref = _oracle_embed(model_path(spec), ids, offs)
