@@ -191,10 +191,15 @@ def run_reference(args, rank):
 
 # ------------------------------------------------------------- work model --
 
+LAYER_CLASSES = ("gemm_qkv", "gemm_attn_out", "gemm_ffn_upgate", "gemm_ffn_down", "attention", "layernorm")
+
+
 def class_work(cls, T, nseq, sum_l2, wtypes, emb_type):
-    """(FLOP, bytes) of one launch of kernel class `cls` over T valid tokens
-    (algorithmic: valid tokens only, weights at their GGUF size, each
-    activation read or written once).  wtypes: GGUF types of (qkv, out,
+    """(FLOP, bytes) of kernel class `cls` for one device call of T valid
+    tokens: per layer for the layer classes (LAYER_CLASSES; the attention
+    class counts all its launches of a layer together), per call for the
+    others.  Algorithmic: valid tokens only, weights at their GGUF size,
+    each activation read or written once.  wtypes: GGUF types of (qkv, out,
     up/gate, down)."""
     fused = T >= 256  # the out and down projections carry the residual LayerNorm
     wb = lambda n, k, t: n * k * BPE[t]  # noqa: E731
@@ -222,21 +227,30 @@ def class_work(cls, T, nseq, sum_l2, wtypes, emb_type):
     return 0.0, 0.0
 
 
-def class_roofline(stats, T, nseq, sum_l2, wtypes, emb_type, pk, sm_mhz=None):
-    """Per kernel class: average launch time, achieved rate, floor and
-    fraction of it (floor = max(FLOP / burst bf16 peak, bytes / HBM peak))."""
+def class_roofline(stats, calls, wtypes, emb_type, pk, sm_mhz=None, steps=1):
+    """Per kernel class over `steps` repetitions of the device calls `calls`
+    [(T, nseq, sum of L^2)]: average launch time, achieved rate and the
+    fraction of the floor (max(FLOP / burst bf16 peak, bytes / HBM peak)) the
+    class's total time reaches."""
     out = {}
     for cls, c in stats["classes"].items():
         if not c["count"]:
             continue
-        avg_s = c["ms"] / c["count"] / 1e3
-        flop, byt = class_work(cls, T, nseq, sum_l2, wtypes, emb_type)
+        flop = byt = 0.0
+        for T, nseq, sl2 in calls:
+            f, b = class_work(cls, T, nseq, sl2, wtypes, emb_type)
+            mult = LAYERS if cls in LAYER_CLASSES else 1
+            flop += f * mult * steps
+            byt += b * mult * steps
+        total_s = c["ms"] / 1e3
         t_flop, t_byte = flop / (pk["tf"] * 1e12), byt / (pk["hbm"] * 1e9)
         tensor = t_flop >= t_byte
-        rec = {"launches": c["count"], "avg_launch_us": avg_s * 1e6, "flop": flop, "bytes": byt,
-               "floor_us": max(t_flop, t_byte) * 1e6, "bound": "tensor" if tensor else "hbm",
-               "frac": max(t_flop, t_byte) / avg_s if avg_s > 0 else None}
-        rec["achieved"] = flop / avg_s / 1e12 if tensor else byt / avg_s / 1e9
+        launches = c["count"]
+        rec = {"launches": launches, "avg_launch_us": total_s / launches * 1e6,
+               "flop_per_launch": flop / launches, "bytes_per_launch": byt / launches,
+               "floor_us_per_launch": max(t_flop, t_byte) / launches * 1e6, "bound": "tensor" if tensor else "hbm",
+               "frac": max(t_flop, t_byte) / total_s if total_s > 0 else None}
+        rec["achieved"] = flop / total_s / 1e12 if tensor else byt / total_s / 1e9
         rec["unit"] = "TFLOP/s" if tensor else "GB/s"
         if tensor and sm_mhz:
             rec["frac_at_sampled_clock"] = rec["frac"] * 1965.0 / sm_mhz
@@ -259,6 +273,7 @@ class DeviceBatch:
         self.sum_l2 = float((self.lens.astype(np.float64) ** 2).sum())
         self.out = torch.empty(max(self.nseq, 1), H, device="cuda")
         self.calls = []
+        self.work = []  # (T, nseq, sum of L^2) of each device call
         s0 = 0
         while s0 < self.nseq:
             s1 = s0 + 1
@@ -268,6 +283,8 @@ class DeviceBatch:
             d_ids = torch.from_numpy(np.ascontiguousarray(ids[offs[s0]:offs[s1]])).cuda()
             d_offs = torch.from_numpy(sub).cuda()
             self.calls.append((d_ids, d_offs, s1 - s0, int(sub[-1]), int(np.diff(sub).max()), s0))
+            lens = np.diff(sub).astype(np.float64)
+            self.work.append((int(sub[-1]), s1 - s0, float((lens ** 2).sum())))
             s0 = s1
 
     def step(self):
@@ -377,7 +394,7 @@ def headline(ctx, args, pk, res):
     assert np.isfinite(out).all()
 
     wtypes, etype = model_types("q8_0")
-    classes = class_roofline(st, b.T, b.nseq, b.sum_l2, wtypes, etype, pk, clk.get("sm_mhz"))
+    classes = class_roofline(st, b.work, wtypes, etype, pk, clk.get("sm_mhz"), steps=args.steps)
     kernel_ms = {k: round(v["ms"] / args.steps, 4) for k, v in st["classes"].items() if v["count"]}
     per_rank = ctx.gather({"rank": ctx.rank, "sequences": [a, b_], "tokens": b.T,
                            "ms_per_step": sum(step_ms) / args.steps, "kernel_ms_per_step": kernel_ms,
@@ -399,8 +416,10 @@ def headline(ctx, args, pk, res):
         d = classes[dom]
         peak = pk["tf"] if d["bound"] == "tensor" else pk["hbm"]
         roof = {"kernel": dom, "bound": d["bound"], "achieved": d["achieved"], "peak": peak, "unit": d["unit"],
-                "frac": d["frac"], "traffic": None, "floor_us": d["floor_us"], "avg_launch_ms": d["avg_launch_us"] / 1e3,
-                "algorithmic_per_launch": {"flop": d["flop"], "bytes": d["bytes"], "tokens": b.T},
+                "frac": d["frac"], "traffic": None, "floor_us": d["floor_us_per_launch"],
+                "avg_launch_ms": d["avg_launch_us"] / 1e3,
+                "algorithmic_per_launch": {"flop": d["flop_per_launch"], "bytes": d["bytes_per_launch"],
+                                           "tokens": b.T},
                 "peak_source": (f"{pk['src']} bf16_tflops (burst: kernel timed inside a sub-second region)"
                                 if d["bound"] == "tensor" else f"{pk['src']} hbm_gbs"),
                 "sm_mhz_sampled": clk.get("sm_mhz")}
@@ -484,7 +503,7 @@ def other_configs(ctx, args, pk, res):
         total = ctx.max(sum(ms))
         st = ctx.profile(b, 1)
         wtypes, etype = model_types(model)
-        classes = class_roofline(st, b.T, b.nseq, b.sum_l2, wtypes, etype, pk)
+        classes = class_roofline(st, b.work, wtypes, etype, pk)
         all_l = np.diff(offs).astype(np.float64)
         flop = GEMM_FLOP_PER_TOKEN * all_l.sum() + 36864.0 * (all_l ** 2).sum()
         t_step = total / steps / 1e3
@@ -492,11 +511,11 @@ def other_configs(ctx, args, pk, res):
             out[key] = {
                 "sequences": int(offs.size - 1), "tokens": int(offs[-1]), "model": model,
                 "ms_per_step": total / steps, "embeddings_per_s": (offs.size - 1) / t_step,
-                "tensor_roofline": {"achieved_tflops": flop / t_step / 1e12, "peak": pk["tf"],
-                                    "frac": flop / t_step / 1e12 / pk["tf"],
+                "tensor_roofline": {"achieved_tflops": flop / t_step / 1e12, "peak": pk["tf"] * ctx.world,
+                                    "frac": flop / t_step / 1e12 / (pk["tf"] * ctx.world),
                                     "flop_per_step": flop,
                                     "note": "GEMM + attention FLOPs of valid tokens over the whole forward "
-                                            "(every kernel, launch gaps included) against burst bf16"},
+                                            "(every kernel, launch gaps included) against burst bf16 x GPUs"},
                 "rank0_kernel_ms": {k: round(v["ms"], 3) for k, v in st["classes"].items() if v["count"]},
                 "rank0_classes": {k: {"frac": v["frac"], "bound": v["bound"]} for k, v in classes.items()},
                 "gpu_launches_per_step": launches / steps,
