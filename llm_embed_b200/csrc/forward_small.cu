@@ -4,8 +4,9 @@
 // At batch 1 the forward is a chain of small dependent steps over 120 MB of
 // weights (Q8_0).  Weights never depend on activations, so each CTA streams
 // the weight pages of its share of every step into a shared-memory ring
-// ahead of use (a producer warp issuing TMA bulk copies, mbarrier-tracked),
-// and the chain itself only waits for the activations other CTAs produce.
+// ahead of use (TMA bulk copies, mbarrier-tracked: thread 0 issues page k + R
+// as soon as the warps are done with page k), and the chain itself only
+// waits for the activations other CTAs produce.
 //
 // Per layer, CTA c:
 //   QKV     LayerNorm of its own copy of the residual stream (every CTA holds
@@ -16,7 +17,9 @@
 //   OUT     (48 CTAs) once all heads are done: an output-projection tile
 //   UG      every CTA, once all output tiles are done: LayerNorm, then its
 //           2-3 up/gate tiles with GEGLU
-//   DOWN    (48 CTAs) once every CTA finished UG: a down-projection tile
+//   DOWN    (144 CTAs) once every CTA finished UG: one K slice of a
+//           down-projection tile (48 tiles x 3 slices of 1,024 columns); the
+//           slices' partial sums are added by the LayerNorm that reads them
 // Each hand-off is a release-add on a counter after the producing tile's
 // stores and an acquire poll by the consumers (bounded: WAIT_LIMIT_NS, then
 // DE_TIMEOUT and every CTA leaves); there is no grid-wide barrier.
@@ -38,7 +41,6 @@ namespace le {
 namespace fs {
 
 using tcx::bulk_load;
-using tcx::mbar_arrive;
 using tcx::mbar_expect_tx;
 using tcx::mbar_init;
 using tcx::mbar_wait;
@@ -47,13 +49,16 @@ constexpr int H = SMALL_HIDDEN;
 constexpr int F = SMALL_FFN;
 constexpr int HEADS = SMALL_HEADS;
 constexpr int HD = H / HEADS;
-constexpr int NCW = r16::WARPS;            // compute warps
-constexpr int NTHREADS = (NCW + 1) * 32;   // + the producer warp
-constexpr int NCT = NCW * 32;              // compute threads (named barrier 1)
+constexpr int NCW = r16::WARPS;            // warps (the K split of gemm_r16.cuh)
+constexpr int NTHREADS = NCW * 32;
+constexpr int NCT = NTHREADS;
 constexpr int LDX = H + 8;                 // padded fp16 row stride of x
-constexpr int PAGE_COLS = 768;             // a page: 16 rows x 768 columns of one tile
-constexpr int PAGE_CHUNKS = PAGE_COLS / TILE_K;
-constexpr int SLOT = PAGE_CHUNKS * r16::chunk_bytes(QF_KMIN);  // 15,360 B: the largest page
+// A page is one work item: a 16-row tile's K slice (gemm_r16.cuh: K = 768 is
+// one slice of 12 chunks, K = 3072 three of 16), contiguous in the row16
+// layout.
+constexpr int MAX_PAGE_CHUNKS = r16::KSLICE / TILE_K;
+constexpr int SLOT = MAX_PAGE_CHUNKS * r16::chunk_bytes(QF_KMIN);  // 20,480 B: the largest page
+constexpr int N_Y2 = 3;                    // K slices of a down-projection tile
 constexpr int ATT_WARP_BYTES = 3 * 16 * attn::LDS * 2;
 constexpr int SMEM_MAX = 232448;
 constexpr int MAX_SLOTS = 16;
@@ -75,16 +80,16 @@ struct Lay {
   static constexpr int X_BYTES = TS * LDX * 2;
   static constexpr int U_BYTES = X_BYTES > NCW * ATT_WARP_BYTES ? X_BYTES : NCW * ATT_WARP_BYTES;
   static constexpr int RED_BYTES = MAX_TILES * NCW * NT * 32 * 16;
-  static constexpr int FIXED = H_BYTES + U_BYTES + RED_BYTES + 2 * MAX_SLOTS * 8 + 64;
+  static constexpr int FIXED = H_BYTES + U_BYTES + RED_BYTES + MAX_SLOTS * 8 + 64;
   static constexpr int R = (SMEM_MAX - FIXED) / SLOT < MAX_SLOTS ? (SMEM_MAX - FIXED) / SLOT : MAX_SLOTS;
   static constexpr int OFF_RING = 0;
   static constexpr int OFF_H = R * SLOT;
   static constexpr int OFF_U = OFF_H + H_BYTES;
   static constexpr int OFF_RED = OFF_U + U_BYTES;
-  static constexpr int OFF_BAR = OFF_RED + RED_BYTES;  // full[R], empty[R]
-  static constexpr int OFF_MISC = OFF_BAR + 2 * R * 8;
+  static constexpr int OFF_BAR = OFF_RED + RED_BYTES;  // full[R]
+  static constexpr int OFF_MISC = OFF_BAR + R * 8;
   static constexpr int BYTES = OFF_MISC + 64;
-  static_assert(R >= 5, "the ring must hold a 4-page tile and the next page");
+  static_assert(R >= MAX_TILES + 1, "the ring must hold a step's pages and the next one");
   static_assert(BYTES <= SMEM_MAX, "shared memory budget");
 };
 
@@ -96,7 +101,7 @@ __device__ __forceinline__ unsigned ld_acquire(const unsigned* p) {
 __device__ __forceinline__ void red_release_add(unsigned* p, unsigned v) {
   asm volatile("red.release.gpu.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
-// Barrier of the compute warps only (the producer warp never joins it).
+// Barrier of the CTA's warps (named barrier 1).
 __device__ __forceinline__ void bar_compute() { asm volatile("bar.sync 1, %0;" ::"n"(NCT) : "memory"); }
 
 // Tiles [t0, t1) of step m for CTA c: an even split, the down projection's
@@ -108,7 +113,13 @@ __device__ __forceinline__ void tile_range(int m, int n_tiles, int* t0, int* t1)
   *t1 = (int)((long)n_tiles * (c + 1) / G);
 }
 __device__ __forceinline__ int att_cta(int head) { return (int)((long)head * gridDim.x / HEADS); }
-__device__ __forceinline__ int pages_of(const SmallGemm& g) { return g.K / PAGE_COLS; }
+// Work items (pages) of step g: its tiles times its K slices; item i is tile
+// i / slices, slice i % slices.
+__device__ __forceinline__ int items_of(const SmallGemm& g) { return g.tiles * r16::n_slices(g.K); }
+__device__ __forceinline__ int page_chunks(const SmallGemm& g, int slice) {
+  const int k0 = slice * r16::KSLICE;
+  return (g.K - k0 < r16::KSLICE ? g.K - k0 : r16::KSLICE) / TILE_K;
+}
 
 template <int R_>
 struct SharedT {
@@ -121,7 +132,6 @@ struct SharedT {
   uint32_t bar0;
   volatile int* abort;
   volatile int* flag;
-  int* pos;
 };
 
 // Compute threads: wait until *c >= target (thread 0 polls with acquire
@@ -163,24 +173,39 @@ __device__ __forceinline__ void signal(const SmallParams& p, int idx) {
 }
 
 // LayerNorm (ops_simd.go:7-24) of h[t] (+ y[t] when y) into h[t] and its fp16
-// copy x[t]; one warp per token row (ln_row_stats order).  Every global load
-// (y, gamma, beta) is issued before the statistics, so the row waits for one
+// copy x[t]; one warp per token row (ln_row_stats order).  y holds `nparts`
+// partial sums (the K slices of the projection, SMALL_MAX_TOKENS rows apart),
+// added in slice order and then to the residual.  Every global load (y,
+// gamma, beta) is issued before the statistics, so the row waits for one
 // memory round trip.
-__device__ void ln_rows(float* h, __half* x, const float* y, const float* w, const float* b, float eps, int T) {
+__device__ void ln_rows(float* h, __half* x, const float* y, const float* w, const float* b, float eps, int T,
+                        int nparts = 1) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   for (int t = warp; t < T; t += NCW) {
-    float4 v[H / 128], wv[H / 128], bv[H / 128];
+    float4 v[H / 128], wv[H / 128], bv[H / 128], yv[N_Y2][H / 128];
 #pragma unroll
     for (int i = 0; i < H / 128; i++) {
       const int c = (i * 32 + lane) * 4;
       wv[i] = __ldg(reinterpret_cast<const float4*>(w + c));
       bv[i] = __ldg(reinterpret_cast<const float4*>(b + c));
-      float4 a = *reinterpret_cast<const float4*>(h + t * H + c);
-      if (y) {
-        const float4 d = __ldcg(reinterpret_cast<const float4*>(y + (long)t * H + c));
-        a = make_float4(__fadd_rn(a.x, d.x), __fadd_rn(a.y, d.y), __fadd_rn(a.z, d.z), __fadd_rn(a.w, d.w));
+      v[i] = *reinterpret_cast<const float4*>(h + t * H + c);
+#pragma unroll
+      for (int q = 0; q < N_Y2; q++)
+        if (y && q < nparts)
+          yv[q][i] = __ldcg(reinterpret_cast<const float4*>(y + (long)q * SMALL_MAX_TOKENS * H + (long)t * H + c));
+    }
+    if (y) {
+#pragma unroll
+      for (int i = 0; i < H / 128; i++) {
+        float4 d = yv[0][i];
+#pragma unroll
+        for (int q = 1; q < N_Y2; q++)
+          if (q < nparts)
+            d = make_float4(__fadd_rn(d.x, yv[q][i].x), __fadd_rn(d.y, yv[q][i].y), __fadd_rn(d.z, yv[q][i].z),
+                            __fadd_rn(d.w, yv[q][i].w));
+        v[i] = make_float4(__fadd_rn(v[i].x, d.x), __fadd_rn(v[i].y, d.y), __fadd_rn(v[i].z, d.z),
+                           __fadd_rn(v[i].w, d.w));
       }
-      v[i] = a;
     }
     float mean, inv;
     ln_row_stats(v, H / 128, H, eps, &mean, &inv);
@@ -292,47 +317,97 @@ __device__ void attention_head(const SmallParams& p, uint8_t* U, int head) {
   }
 }
 
-// Tiles t0 .. t0+nt-1 (nt <= MAX_TILES) of step g, whose pages sit at ring
-// positions seq0.. of the page sequence: every warp runs its units of every
-// tile (the B operand fragments loaded once per unit and shared by the
-// tiles), then the partials, the reduction and the epilogue of all tiles.
+// The CTA's page sequence (every step's work items in consumption order),
+// walked by thread 0 as it issues the pages' bulk copies: page k goes to ring
+// slot k % R once page k - R has been consumed.
+struct PageIter {
+  int l = 0, m = 0, it = 0, t1 = -1;
+  uint32_t issued = 0;  // pages issued so far
+};
+
+// Issue the next page of the sequence into its slot (thread 0); false when
+// the sequence is exhausted.
+template <class SH>
+__device__ bool issue_next(const SmallParams& p, const SH& S, PageIter& pi) {
+  while (pi.l < p.n_layers) {
+    const SmallGemm& g = p.layers[pi.l].g[pi.m];
+    if (pi.t1 < 0) tile_range(pi.m, items_of(g), &pi.it, &pi.t1);
+    if (pi.it < pi.t1) {
+      const int ns = r16::n_slices(g.K), tile = pi.it / ns, slice = pi.it % ns;
+      const uint32_t slot = pi.issued % SH::R;
+      const uint32_t bytes = page_chunks(g, slice) * r16::chunk_bytes(g.qf);
+      const uint8_t* src = g.w + (long)tile * (g.K / TILE_K) * r16::chunk_bytes(g.qf) +
+                           (long)slice * (r16::KSLICE / TILE_K) * r16::chunk_bytes(g.qf);
+      mbar_expect_tx(S.bar0 + 8 * slot, bytes);
+      bulk_load(tcx::smem_u32(S.ring + slot * SLOT), src, bytes, S.bar0 + 8 * slot);
+      pi.it++;
+      pi.issued++;
+      return true;
+    }
+    pi.t1 = -1;
+    if (++pi.m == 4) {
+      pi.m = 0;
+      pi.l++;
+    }
+  }
+  return false;
+}
+
+// Thread 0 before the CTA exits: every issued copy has landed (a CTA must not
+// exit with bulk copies into its shared memory in flight).
+template <class SH>
+__device__ void drain(const SH& S, const PageIter& pi) {
+  const uint32_t first = pi.issued > (uint32_t)SH::R ? pi.issued - SH::R : 0;
+  volatile int no_abort = 0;
+  for (uint32_t sq = first; sq < pi.issued; sq++)
+    mbar_wait(S.bar0 + 8 * (sq % SH::R), (sq / SH::R) & 1, &no_abort, nullptr, 62);
+}
+
+// Work items it0 .. it0+n-1 (n <= MAX_TILES) of step g, one page each at
+// ring positions seq0.. of the page sequence (the items of one call are K
+// slices of equal size): every warp runs its units of every item (the B
+// operand fragments loaded once per unit and shared by the items), then the
+// partials, the reduction and the epilogue of all items.  An item of a
+// sliced step (K > 1024) writes its slice's partial sums to
+// ep.out32 + slice * SMALL_MAX_TOKENS * ldo; the reader adds the slices.
 // B operand: x in shared memory (xs, stride LDX) or a global fp16 matrix
 // (xg, stride ldg; all of the warp's fragments are loaded before the first
 // MMA, one memory round trip).  For EPI_QKV the RoPE cos/sin of each output
 // item come preloaded in rc/rs (item i < 64 NT of the first tile).  Returns
 // false if a page wait failed.
 template <int QF, int NT, int UMAX, bool GB, class SH>
-__device__ bool gemm_tiles(const SmallParams& p, const SH& S, const SmallGemm& g, int t0, int nt, uint32_t seq0,
-                           const __half* xs, const __half* xg, int ldg, const EpiParams& ep, float rc, float rs) {
+__device__ bool gemm_tiles(const SmallParams& p, const SH& S, PageIter& pi, const SmallGemm& g, int it0, int n,
+                           uint32_t seq0, const __half* xs, const __half* xg, int ldg, const EpiParams& ep, float rc,
+                           float rs) {
   const int w = threadIdx.x >> 5, lane = threadIdx.x & 31, gi = lane >> 2, ti = lane & 3;
-  const int npg = pages_of(g);
+  const int ns = r16::n_slices(g.K);
+  const int slice0 = it0 % ns;
   int u0, u1;
-  r16::warp_units(g.K, w, &u0, &u1);
+  r16::slice_units(g.K, slice0, w, &u0, &u1);  // the same count in every item of the call
+  const int ubase = slice0 * (r16::KSLICE / 32);
   // B fragments from global memory first: their latency overlaps the page waits.
   uint4 bq[GB ? UMAX : 1][NT];
   if constexpr (GB) {
 #pragma unroll
     for (int i = 0; i < UMAX; i++)
 #pragma unroll
-      for (int n = 0; n < NT; n++) {
-        const int u = u0 + i, m = 8 * n + gi;
+      for (int nn = 0; nn < NT; nn++) {
+        const int u = u0 + i, m = 8 * nn + gi;
         const int k = (u >> 1) * TILE_K + 16 * ti + 8 * (u & 1);
-        bq[i][n] = (u < u1 && m < p.T) ? __ldcg(reinterpret_cast<const uint4*>(xg + (long)m * ldg + k))
-                                       : make_uint4(0, 0, 0, 0);
+        bq[i][nn] = (u < u1 && m < p.T) ? __ldcg(reinterpret_cast<const uint4*>(xg + (long)m * ldg + k))
+                                        : make_uint4(0, 0, 0, 0);
       }
   }
   bool ok = true;
-  const int pg0 = (u0 >> 1) / PAGE_CHUNKS, pg1 = ((u1 - 1) >> 1) / PAGE_CHUNKS;
-  for (int i = 0; i < nt && ok; i++)
-    for (int pg = pg0; pg <= pg1 && ok; pg++) {
-      const uint32_t sq = seq0 + i * npg + pg;
-      ok = mbar_wait(S.bar0 + 8 * (sq % S.R), (sq / S.R) & 1, S.abort, p.status, 60);
-    }
+  for (int i = 0; i < n && ok; i++) {
+    const uint32_t sq = seq0 + i;
+    ok = mbar_wait(S.bar0 + 8 * (sq % SH::R), (sq / SH::R) & 1, S.abort, p.status, 60);
+  }
   float acc[MAX_TILES][NT][4];
 #pragma unroll
   for (int i = 0; i < MAX_TILES; i++)
 #pragma unroll
-    for (int n = 0; n < NT; n++) acc[i][n][0] = acc[i][n][1] = acc[i][n][2] = acc[i][n][3] = 0.f;
+    for (int nn = 0; nn < NT; nn++) acc[i][nn][0] = acc[i][nn][1] = acc[i][nn][2] = acc[i][nn][3] = 0.f;
   if (ok) {
 #pragma unroll
     for (int i = 0; i < UMAX; i++) {
@@ -340,96 +415,72 @@ __device__ bool gemm_tiles(const SmallParams& p, const SH& S, const SmallGemm& g
       if (u >= u1) break;
       const int c = u >> 1, hf = u & 1;
       const int k = c * TILE_K + 16 * ti + 8 * hf;
+      const int cl = (u - ubase) >> 1;  // chunk within the item's page
       uint4 b[NT];
 #pragma unroll
-      for (int n = 0; n < NT; n++)
-        b[n] = GB ? bq[GB ? i : 0][n] : *reinterpret_cast<const uint4*>(xs + (8 * n + gi) * LDX + k);
+      for (int nn = 0; nn < NT; nn++)
+        b[nn] = GB ? bq[GB ? i : 0][nn] : *reinterpret_cast<const uint4*>(xs + (8 * nn + gi) * LDX + k);
 #pragma unroll
       for (int tt = 0; tt < MAX_TILES; tt++) {
-        if (tt >= nt) break;
-        const uint32_t sq = seq0 + tt * npg + c / PAGE_CHUNKS;
-        const uint8_t* chunk = S.ring + (sq % S.R) * SLOT + (c % PAGE_CHUNKS) * r16::chunk_bytes(QF);
+        if (tt >= n) break;
+        const uint32_t sq = seq0 + tt;
+        const uint8_t* chunk = S.ring + (sq % SH::R) * SLOT + cl * r16::chunk_bytes(QF);
         const uint2 qa = *reinterpret_cast<const uint2*>(chunk + gi * TILE_K + 16 * ti + 8 * hf);
         const uint2 qb = *reinterpret_cast<const uint2*>(chunk + (gi + 8) * TILE_K + 16 * ti + 8 * hf);
         const uint4 ha = dq8_f16<QF>(qa, chunk + r16::CHUNK_Q, gi, 2 * ti + hf);
         const uint4 hb = dq8_f16<QF>(qb, chunk + r16::CHUNK_Q, gi + 8, 2 * ti + hf);
 #pragma unroll
-        for (int n = 0; n < NT; n++) {
-          r16::mma16816(acc[tt][n], ha.x, hb.x, ha.y, hb.y, b[n].x, b[n].y);
-          r16::mma16816(acc[tt][n], ha.z, hb.z, ha.w, hb.w, b[n].z, b[n].w);
+        for (int nn = 0; nn < NT; nn++) {
+          r16::mma16816(acc[tt][nn], ha.x, hb.x, ha.y, hb.y, b[nn].x, b[nn].y);
+          r16::mma16816(acc[tt][nn], ha.z, hb.z, ha.w, hb.w, b[nn].z, b[nn].w);
         }
       }
     }
   }
 #pragma unroll
   for (int tt = 0; tt < MAX_TILES; tt++)
-    if (tt < nt) r16::store_partials<NT>(S.red + tt * NCW * NT * 32, acc[tt]);
+    if (tt < n) r16::store_partials<NT>(S.red + tt * NCW * NT * 32, acc[tt]);
   bar_compute();
-  // The tiles' pages are free again: one arrival per warp on each.
-  if (lane == 0)
-    for (int q = 0; q < nt * npg; q++) mbar_arrive(S.bar0 + 8 * (S.R + (seq0 + q) % S.R));
+  // The items' pages are consumed: their slots take the next pages (the
+  // proxy fence orders the warps' reads before the copies' writes).
+  if (threadIdx.x == 0) {
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    for (int q = 0; q < n; q++) issue_next(p, S, pi);
+  }
   if (*S.abort) return false;
-  for (int i = threadIdx.x; i < 64 * NT * nt; i += NCT) {
+  for (int i = threadIdx.x; i < 64 * NT * n; i += NCT) {
     const int tt = i / (64 * NT), it = i % (64 * NT);
+    const int item = it0 + tt, tile = item / ns, slice = item % ns;
     int q, m;
     float va, vb;
     r16::reduce_item<NT>(S.red + tt * NCW * NT * 32, it, &q, &m, &va, &vb);
     if (m >= p.T) continue;
-    const int a = r16::pair_virtual_row(g.mode, t0 + tt, q);
+    const int a = r16::pair_virtual_row(g.mode, tile, q);
     if (ep.mode == EPI_QKV && a < ep.rope_cols) {
       // epi_pair's RoPE with the preloaded table values.
       const float x0 = __fsub_rn(__fmul_rn(va, rc), __fmul_rn(vb, rs));
       const float x1 = __fadd_rn(__fmul_rn(va, rs), __fmul_rn(vb, rc));
       *reinterpret_cast<uint32_t*>(ep.out16 + (long)m * ep.ldo + a) = pack_half2(x0, x1);
+    } else if (ns > 1) {
+      float* o = ep.out32 + (long)slice * SMALL_MAX_TOKENS * ep.ldo + (long)m * ep.ldo;
+      *reinterpret_cast<float2*>(o + a) = make_float2(va, vb);
     } else {
       epi_pair(ep, m, a, va, vb);
     }
   }
-  bar_compute();  // the partials buffer is free for the next tiles
+  bar_compute();  // the partials buffer is free for the next items
   return true;
 }
 
 template <int NT, int UMAX, bool GB, class SH>
-__device__ bool gemm_tiles_any(const SmallParams& p, const SH& S, const SmallGemm& g, int t0, int nt,
+__device__ bool gemm_tiles_any(const SmallParams& p, const SH& S, PageIter& pi, const SmallGemm& g, int t0, int nt,
                                uint32_t seq0, const __half* xs, const __half* xg, int ldg, const EpiParams& ep,
                                float rc = 0.f, float rs = 0.f) {
   switch (g.qf) {
-    case QF_Q8_0: return gemm_tiles<QF_Q8_0, NT, UMAX, GB, SH>(p, S, g, t0, nt, seq0, xs, xg, ldg, ep, rc, rs);
-    case QF_KMIN: return gemm_tiles<QF_KMIN, NT, UMAX, GB, SH>(p, S, g, t0, nt, seq0, xs, xg, ldg, ep, rc, rs);
-    default: return gemm_tiles<QF_Q6K, NT, UMAX, GB, SH>(p, S, g, t0, nt, seq0, xs, xg, ldg, ep, rc, rs);
+    case QF_Q8_0: return gemm_tiles<QF_Q8_0, NT, UMAX, GB, SH>(p, S, pi, g, t0, nt, seq0, xs, xg, ldg, ep, rc, rs);
+    case QF_KMIN: return gemm_tiles<QF_KMIN, NT, UMAX, GB, SH>(p, S, pi, g, t0, nt, seq0, xs, xg, ldg, ep, rc, rs);
+    default: return gemm_tiles<QF_Q6K, NT, UMAX, GB, SH>(p, S, pi, g, t0, nt, seq0, xs, xg, ldg, ep, rc, rs);
   }
-}
-
-// The producer: every page of this CTA's share of every step, in the order
-// the compute warps consume them, into the ring (TMA bulk copies).
-template <class SH>
-__device__ void producer(const SmallParams& p, const SH& S) {
-  if ((threadIdx.x & 31) != 0) return;
-  uint32_t seq = 0;
-  bool ok = true;
-  for (int l = 0; l < p.n_layers && ok; l++) {
-    for (int m = 0; m < 4 && ok; m++) {
-      const SmallGemm& g = p.layers[l].g[m];
-      int t0, t1;
-      tile_range(m, g.tiles, &t0, &t1);
-      const uint32_t bytes = PAGE_CHUNKS * r16::chunk_bytes(g.qf);
-      for (int t = t0; t < t1 && ok; t++) {
-        for (int pg = 0; pg < pages_of(g) && ok; pg++, seq++) {
-          const uint32_t slot = seq % S.R, use = seq / S.R;
-          if (use > 0) ok = mbar_wait(S.bar0 + 8 * (S.R + slot), (use - 1) & 1, S.abort, p.status, 61);
-          if (!ok) break;
-          const uint8_t* src = g.w + (long)t * (g.K / TILE_K) * r16::chunk_bytes(g.qf) + (long)pg * bytes;
-          mbar_expect_tx(S.bar0 + 8 * slot, bytes);
-          bulk_load(tcx::smem_u32(S.ring + slot * SLOT), src, bytes, S.bar0 + 8 * slot);
-        }
-      }
-    }
-  }
-  // Copies still in flight (after a failure) must land before the CTA exits.
-  const uint32_t first = seq > (uint32_t)S.R ? seq - S.R : 0;
-  volatile int no_abort = 0;
-  for (uint32_t sq = first; sq < seq; sq++)
-    mbar_wait(S.bar0 + 8 * (sq % S.R), (sq / S.R) & 1, &no_abort, nullptr, 62);
 }
 
 template <int NT>
@@ -447,19 +498,15 @@ __global__ void __launch_bounds__(NTHREADS, 1) forward_small_kernel(const __grid
   S.flag = reinterpret_cast<volatile int*>(smem + L::OFF_MISC + 4);
   const int T = p.T;
 
+  PageIter pi;
   if (threadIdx.x == 0) {
-    for (int i = 0; i < L::R; i++) {
-      mbar_init(S.bar0 + 8 * i, 1);
-      mbar_init(S.bar0 + 8 * (L::R + i), NCW);
-    }
+    for (int i = 0; i < L::R; i++) mbar_init(S.bar0 + 8 * i, 1);
     *S.abort = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    for (int i = 0; i < L::R; i++)
+      if (!issue_next(p, S, pi)) break;
   }
   __syncthreads();
-  if (threadIdx.x >= NCT) {
-    producer(p, S);
-    return;
-  }
 
   // Token positions inside their sequences (every CTA writes the same values).
   prefetch_small(p);
@@ -487,9 +534,8 @@ __global__ void __launch_bounds__(NTHREADS, 1) forward_small_kernel(const __grid
       // before the wait.
       float rc = 0.f, rs = 0.f;
       if (t1 > t0 && threadIdx.x < 64 * NT) {
-        int q, m;
-        q = (threadIdx.x & 63) >> 3;
-        m = 8 * (threadIdx.x >> 6) + 2 * ((threadIdx.x >> 1) & 3) + (threadIdx.x & 1);
+        const int q = (threadIdx.x & 63) >> 3;
+        const int m = 8 * (threadIdx.x >> 6) + 2 * ((threadIdx.x >> 1) & 3) + (threadIdx.x & 1);
         const int a = 16 * t0 + 2 * q;
         if (m < T && a < 2 * H) {
           const long r = (long)p.pos[m] * (HD / 2) + ((a % HD) >> 1);
@@ -498,8 +544,9 @@ __global__ void __launch_bounds__(NTHREADS, 1) forward_small_kernel(const __grid
         }
       }
       if (l > 0) {
-        if (!wait_cnt(p, S, CNT_Y2, (unsigned)(p.layers[0].g[3].tiles * l), 70)) return;
-        ln_rows(S.h, S.x, p.y2, p.layers[l - 1].out_w, p.layers[l - 1].out_b, p.eps, T);
+        const SmallGemm& prev = p.layers[l - 1].g[3];
+        if (!wait_cnt(p, S, CNT_Y2, (unsigned)(items_of(prev) * l), 70)) goto out;
+        ln_rows(S.h, S.x, p.y2, p.layers[l - 1].out_w, p.layers[l - 1].out_b, p.eps, T, r16::n_slices(prev.K));
         bar_compute();
       }
       EpiParams ep{};
@@ -515,20 +562,19 @@ __global__ void __launch_bounds__(NTHREADS, 1) forward_small_kernel(const __grid
       ep.rope_cols = 2 * H;
       for (int t = t0; t < t1; t++) {
         // RoPE values preloaded for the first tile only.
-        const bool pre = t == t0;
-        if (pre) {
-          if (!gemm_tiles_any<NT, 3, false>(p, S, g, t, 1, seq, S.x, nullptr, 0, ep, rc, rs)) return;
+        if (t == t0) {
+          if (!gemm_tiles_any<NT, 3, false>(p, S, pi, g, t, 1, seq, S.x, nullptr, 0, ep, rc, rs)) goto out;
         } else {
-          if (!gemm_tiles_any<NT, 3, false>(p, S, g, t, 1, seq, S.x, nullptr, 0, ep, 0.f, 0.f)) return;
+          if (!gemm_tiles_any<NT, 3, false>(p, S, pi, g, t, 1, seq, S.x, nullptr, 0, ep)) goto out;
         }
-        seq += pages_of(g);
+        seq += 1;
         signal(p, CNT_QKV + ((16 * t) % H) / HD);
       }
     }
     // ---- Attention of one head, once its 12 QKV tiles are in.
     for (int hd = 0; hd < HEADS; hd++) {
       if (att_cta(hd) != (int)blockIdx.x) continue;
-      if (!wait_cnt(p, S, CNT_QKV + hd, (unsigned)(3 * HD / 16 * (l + 1)), 71)) return;
+      if (!wait_cnt(p, S, CNT_QKV + hd, (unsigned)(3 * HD / 16 * (l + 1)), 71)) goto out;
       attention_head(p, S.U, hd);
       signal(p, CNT_ATT);
     }
@@ -536,8 +582,8 @@ __global__ void __launch_bounds__(NTHREADS, 1) forward_small_kernel(const __grid
     {
       const SmallGemm& g = Ly.g[1];
       int t0, t1;
-      tile_range(1, g.tiles, &t0, &t1);
-      if (t1 > t0 && !wait_cnt(p, S, CNT_ATT, (unsigned)(HEADS * (l + 1)), 72)) return;
+      tile_range(1, items_of(g), &t0, &t1);
+      if (t1 > t0 && !wait_cnt(p, S, CNT_ATT, (unsigned)(HEADS * (l + 1)), 72)) goto out;
       EpiParams ep{};
       ep.M = T;
       ep.mode = EPI_F32;
@@ -545,14 +591,14 @@ __global__ void __launch_bounds__(NTHREADS, 1) forward_small_kernel(const __grid
       ep.out32 = p.y1;
       ep.ldo = H;
       for (int t = t0; t < t1; t++) {
-        if (!gemm_tiles_any<NT, 3, true>(p, S, g, t, 1, seq, nullptr, p.att, H, ep)) return;
-        seq += pages_of(g);
+        if (!gemm_tiles_any<NT, 3, true>(p, S, pi, g, t, 1, seq, nullptr, p.att, H, ep)) goto out;
+        seq += 1;
         signal(p, CNT_Y1);
       }
     }
     // ---- Up/gate: residual LayerNorm after attention, GEGLU tiles.
     {
-      if (!wait_cnt(p, S, CNT_Y1, (unsigned)(Ly.g[1].tiles * (l + 1)), 73)) return;
+      if (!wait_cnt(p, S, CNT_Y1, (unsigned)(items_of(Ly.g[1]) * (l + 1)), 73)) goto out;
       ln_rows(S.h, S.x, p.y1, Ly.attn_w, Ly.attn_b, p.eps, T);
       bar_compute();
       EpiParams ep{};
@@ -563,20 +609,21 @@ __global__ void __launch_bounds__(NTHREADS, 1) forward_small_kernel(const __grid
       ep.ldo = F;
       const SmallGemm& g = Ly.g[2];
       int t0, t1;
-      tile_range(2, g.tiles, &t0, &t1);
+      tile_range(2, items_of(g), &t0, &t1);
       for (int t = t0; t < t1; t += MAX_TILES) {
         const int n = t1 - t < MAX_TILES ? t1 - t : MAX_TILES;
-        if (!gemm_tiles_any<NT, 3, false>(p, S, g, t, n, seq, S.x, nullptr, 0, ep)) return;
-        seq += n * pages_of(g);
+        if (!gemm_tiles_any<NT, 3, false>(p, S, pi, g, t, n, seq, S.x, nullptr, 0, ep)) goto out;
+        seq += n;
       }
       signal(p, CNT_FF);
     }
-    // ---- Down projection tiles, once every CTA finished up/gate.
+    // ---- Down projection: (tile, K slice) items, one page each, once every
+    // CTA finished up/gate; the next LayerNorm adds the slices' partial sums.
     {
       const SmallGemm& g = Ly.g[3];
       int t0, t1;
-      tile_range(3, g.tiles, &t0, &t1);
-      if (t1 > t0 && !wait_cnt(p, S, CNT_FF, (unsigned)(G * (l + 1)), 74)) return;
+      tile_range(3, items_of(g), &t0, &t1);
+      if (t1 > t0 && !wait_cnt(p, S, CNT_FF, (unsigned)(G * (l + 1)), 74)) goto out;
       EpiParams ep{};
       ep.M = T;
       ep.mode = EPI_F32;
@@ -584,20 +631,23 @@ __global__ void __launch_bounds__(NTHREADS, 1) forward_small_kernel(const __grid
       ep.out32 = p.y2;
       ep.ldo = H;
       for (int t = t0; t < t1; t++) {
-        if (!gemm_tiles_any<NT, 12, true>(p, S, g, t, 1, seq, nullptr, p.ff, F, ep)) return;
-        seq += pages_of(g);
+        if (!gemm_tiles_any<NT, 4, true>(p, S, pi, g, t, 1, seq, nullptr, p.ff, F, ep)) goto out;
+        seq += 1;
         signal(p, CNT_Y2);
       }
     }
   }
   // Final residual LayerNorm; one CTA writes h for the pooling kernel.
   if (blockIdx.x == 0) {
-    const SmallLayer& last = p.layers[p.n_layers - 1];
-    if (!wait_cnt(p, S, CNT_Y2, (unsigned)(last.g[3].tiles * p.n_layers), 75)) return;
-    ln_rows(S.h, S.x, p.y2, last.out_w, last.out_b, p.eps, T);
+    const SmallGemm& last = p.layers[p.n_layers - 1].g[3];
+    if (!wait_cnt(p, S, CNT_Y2, (unsigned)(items_of(last) * p.n_layers), 75)) goto out;
+    ln_rows(S.h, S.x, p.y2, p.layers[p.n_layers - 1].out_w, p.layers[p.n_layers - 1].out_b, p.eps, T,
+            r16::n_slices(last.K));
     bar_compute();
     for (int i = threadIdx.x; i < T * H; i += NCT) p.h_out[i] = S.h[i];
   }
+out:
+  if (threadIdx.x == 0) drain(S, pi);
 }
 
 }  // namespace fs
@@ -609,7 +659,9 @@ bool small_forward_supported(const SmallParams& p, int hidden, int ffn, int head
   for (int l = 0; l < p.n_layers; l++)
     for (int m = 0; m < 4; m++) {
       const SmallGemm& g = p.layers[l].g[m];
-      if (!g.w || g.K % fs::PAGE_COLS || (g.qf != QF_Q8_0 && g.qf != QF_KMIN && g.qf != QF_Q6K)) return false;
+      if (!g.w || g.K % TILE_K || r16::n_slices(g.K) > (m == 3 ? fs::N_Y2 : 1) ||
+          (g.qf != QF_Q8_0 && g.qf != QF_KMIN && g.qf != QF_Q6K))
+        return false;
       const int want = m == 0 ? 3 * SMALL_HIDDEN / 16 : m == 2 ? SMALL_FFN / 8 : SMALL_HIDDEN / 16;
       if (g.tiles != want) return false;
     }

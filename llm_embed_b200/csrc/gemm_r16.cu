@@ -4,6 +4,8 @@
 // whole DRAM traffic, read once; each thread streams 8 bytes per weight row
 // per unit straight from global memory into its fragment, dequantised in
 // registers to the fp16 operand values every GEMM path uses.
+#include <mutex>
+
 #include "gemm_r16.cuh"
 #include "kernels.h"
 
@@ -13,16 +15,11 @@ namespace {
 template <int QF, int NT>
 __global__ void __launch_bounds__(256) gemm_r16_kernel(const uint8_t* __restrict__ W, int n_tiles, int K,
                                                        const __half* __restrict__ A, long lda, EpiParams ep) {
-  __shared__ float4 red[r16::WARPS * NT * 32];
+  extern __shared__ float4 red[];  // [slices][8 warps][NT][32 lanes]
   const int j = blockIdx.x;
   const int w = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2;
   pdl_wait();
-  float acc[NT][4];
-#pragma unroll
-  for (int nt = 0; nt < NT; nt++) acc[nt][0] = acc[nt][1] = acc[nt][2] = acc[nt][3] = 0.f;
-  int u0, u1;
-  r16::warp_units(K, w, &u0, &u1);
-  const int M = ep.M;
+  const int M = ep.M, ns = r16::n_slices(K);
   auto bload = [&](int nt, int k) -> uint4 {
     const int m = 8 * nt + g;
     if (m >= M) return make_uint4(0, 0, 0, 0);
@@ -30,16 +27,47 @@ __global__ void __launch_bounds__(256) gemm_r16_kernel(const uint8_t* __restrict
   };
   const uint8_t* tile = W + (long)j * r16::tile_bytes(QF, K);
   auto chunk_at = [&](int c) { return tile + (long)c * r16::chunk_bytes(QF); };
-  r16::tile_units<QF, NT>(chunk_at, u0, u1, acc, bload);
-  r16::store_partials<NT>(red, acc);
+  for (int s = 0; s < ns; s++) {
+    float acc[NT][4];
+#pragma unroll
+    for (int nt = 0; nt < NT; nt++) acc[nt][0] = acc[nt][1] = acc[nt][2] = acc[nt][3] = 0.f;
+    int u0, u1;
+    r16::slice_units(K, s, w, &u0, &u1);
+    r16::tile_units<QF, NT>(chunk_at, u0, u1, acc, bload);
+    r16::store_partials<NT>(red + s * r16::WARPS * NT * 32, acc);
+  }
   __syncthreads();
   pdl_trigger();
   for (int i = threadIdx.x; i < 64 * NT; i += blockDim.x) {
     int q, m;
     float va, vb;
-    r16::reduce_item<NT>(red, i, &q, &m, &va, &vb);
+    r16::reduce_item<NT>(red, i, &q, &m, &va, &vb, ns);
     if (m < M) epi_pair(ep, m, r16::pair_virtual_row(ep.mode, j, q), va, vb);
   }
+}
+
+// One launch with the partials of all K slices in dynamic shared memory
+// (the attribute for MAX_SLICES slices set once per device).
+template <int QF, int NT>
+cudaError_t launch_nt(const cudaLaunchConfig_t& cfg0, const uint8_t* W, int n_tiles, int K, const __half* A, long lda,
+                      const EpiParams& ep) {
+  cudaLaunchConfig_t cfg = cfg0;
+  cfg.dynamicSmemBytes = (size_t)r16::n_slices(K) * r16::WARPS * NT * 32 * sizeof(float4);
+  static std::mutex mu;
+  static bool done[64] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev >= 64) return cudaErrorInvalidDevice;
+  {
+    std::lock_guard<std::mutex> lk(mu);
+    if (!done[dev]) {
+      const cudaError_t e = cudaFuncSetAttribute(gemm_r16_kernel<QF, NT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                 (int)(r16::MAX_SLICES * r16::WARPS * NT * 32 * sizeof(float4)));
+      if (e != cudaSuccess) return e;
+      done[dev] = true;
+    }
+  }
+  return cudaLaunchKernelEx(&cfg, gemm_r16_kernel<QF, NT>, W, n_tiles, K, A, lda, ep);
 }
 
 template <int QF>
@@ -49,14 +77,14 @@ cudaError_t launch_qf(const uint8_t* W, int n_tiles, int K, const __half* A, lon
   cudaLaunchAttribute attr[1];
   const cudaLaunchConfig_t cfg = pdl_config(dim3(n_tiles), dim3(256), 0, s, attr);
   switch (nt) {
-    case 1: return cudaLaunchKernelEx(&cfg, gemm_r16_kernel<QF, 1>, W, n_tiles, K, A, lda, ep);
-    case 2: return cudaLaunchKernelEx(&cfg, gemm_r16_kernel<QF, 2>, W, n_tiles, K, A, lda, ep);
-    case 3: return cudaLaunchKernelEx(&cfg, gemm_r16_kernel<QF, 3>, W, n_tiles, K, A, lda, ep);
-    case 4: return cudaLaunchKernelEx(&cfg, gemm_r16_kernel<QF, 4>, W, n_tiles, K, A, lda, ep);
-    case 5: return cudaLaunchKernelEx(&cfg, gemm_r16_kernel<QF, 5>, W, n_tiles, K, A, lda, ep);
-    case 6: return cudaLaunchKernelEx(&cfg, gemm_r16_kernel<QF, 6>, W, n_tiles, K, A, lda, ep);
-    case 7: return cudaLaunchKernelEx(&cfg, gemm_r16_kernel<QF, 7>, W, n_tiles, K, A, lda, ep);
-    case 8: return cudaLaunchKernelEx(&cfg, gemm_r16_kernel<QF, 8>, W, n_tiles, K, A, lda, ep);
+    case 1: return launch_nt<QF, 1>(cfg, W, n_tiles, K, A, lda, ep);
+    case 2: return launch_nt<QF, 2>(cfg, W, n_tiles, K, A, lda, ep);
+    case 3: return launch_nt<QF, 3>(cfg, W, n_tiles, K, A, lda, ep);
+    case 4: return launch_nt<QF, 4>(cfg, W, n_tiles, K, A, lda, ep);
+    case 5: return launch_nt<QF, 5>(cfg, W, n_tiles, K, A, lda, ep);
+    case 6: return launch_nt<QF, 6>(cfg, W, n_tiles, K, A, lda, ep);
+    case 7: return launch_nt<QF, 7>(cfg, W, n_tiles, K, A, lda, ep);
+    case 8: return launch_nt<QF, 8>(cfg, W, n_tiles, K, A, lda, ep);
     default: return cudaErrorInvalidValue;
   }
 }
@@ -69,7 +97,8 @@ cudaError_t launch_qf(const uint8_t* W, int n_tiles, int K, const __half* A, lon
 cudaError_t launch_gemm_r16(int qf, const uint8_t* W, int n_tiles, int K, const __half* A, long lda,
                             const EpiParams& ep, cudaStream_t s) {
   if (ep.M == 0) return cudaSuccess;
-  if (K % TILE_K || (lda * 2) % 16 || (reinterpret_cast<uintptr_t>(A) & 15) || n_tiles <= 0)
+  if (K % TILE_K || K > r16::MAX_SLICES * r16::KSLICE || (lda * 2) % 16 || (reinterpret_cast<uintptr_t>(A) & 15) ||
+      n_tiles <= 0)
     return cudaErrorInvalidValue;
   for (int m0 = 0; m0 < ep.M; m0 += 64) {
     EpiParams e = ep;

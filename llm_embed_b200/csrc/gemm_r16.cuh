@@ -23,11 +23,16 @@
 // x . W^T; a thread reads its 8 weight bytes per row and 8 fp16 activations
 // per token with one load each.
 //
-// K split.  The K/32 units (chunk u/2, half u%2) are divided evenly over the
-// 8 warps of a CTA in order; each warp accumulates its units in order into
-// its own fragments, and the eight partial fragments are summed warp 0..7 in
-// float32.  Both kernels use exactly this split and order, for every token
-// count, so a token's output never depends on the other tokens in the call.
+// K split.  K is cut into slices of KSLICE = 1024 columns (the last may be
+// shorter: K = 768 is one slice, K = 3072 three).  In each slice the K/32
+// units (chunk u/2, half u%2) are divided evenly over the 8 warps of a CTA in
+// order; each warp accumulates its units in order into its own fragments,
+// the eight partial fragments are summed warp 0..7 in float32, and the
+// slices' sums are added slice 0, 1, ... in float32.  Both kernels use
+// exactly this split and order, for every token count (the batch-1 kernel
+// computes the slices of a tile on different CTAs and adds them where they
+// are read), so a token's output never depends on the other tokens in the
+// call.
 #pragma once
 #include "dequant.cuh"
 #include "epilogue.cuh"
@@ -43,11 +48,17 @@ __host__ __device__ constexpr int meta_row_bytes(int qf) { return qf == QF_Q8_0 
 __host__ __device__ constexpr int chunk_bytes(int qf) { return CHUNK_Q + ROWS * meta_row_bytes(qf); }
 __host__ __device__ constexpr long tile_bytes(int qf, int K) { return (long)(K / TILE_K) * chunk_bytes(qf); }
 
-// Units [u0, u1) of warp w for a K-column tile.
-__device__ __forceinline__ void warp_units(int K, int w, int* u0, int* u1) {
-  const int U = K / 32;
-  *u0 = w * U / WARPS;
-  *u1 = (w + 1) * U / WARPS;
+constexpr int KSLICE = 1024;
+constexpr int MAX_SLICES = 4;  // K <= 4096
+__host__ __device__ constexpr int n_slices(int K) { return (K + KSLICE - 1) / KSLICE; }
+
+// Units [u0, u1) (absolute unit indices) of warp w in slice s of a K-column
+// tile.
+__device__ __forceinline__ void slice_units(int K, int s, int w, int* u0, int* u1) {
+  const int k0 = s * KSLICE, ks = K - k0 < KSLICE ? K - k0 : KSLICE;
+  const int U = ks / 32, base = k0 / 32;
+  *u0 = base + w * U / WARPS;
+  *u1 = base + (w + 1) * U / WARPS;
 }
 
 __device__ __forceinline__ void mma16816(float* c, uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0,
@@ -93,24 +104,32 @@ __device__ __forceinline__ void store_partials(float4* red, const float (&acc)[N
     red[(w * NT + nt) * 32 + lane] = make_float4(acc[nt][0], acc[nt][1], acc[nt][2], acc[nt][3]);
 }
 
-// Output item i (< 64 * NT) of a tile after store_partials: the pair index
-// q (0..7, the tile's row pair), the token and the two sums over the warps
-// in order 0..7.
+// Output item i (< 64 * NT) of a tile after store_partials of its `ns`
+// slices (slice s at red + s * WARPS * NT * 32): the pair index q (0..7, the
+// tile's row pair), the token and the two sums: over the warps in order
+// 0..7 per slice, then the slices in order.
 template <int NT>
-__device__ __forceinline__ void reduce_item(const float4* red, int i, int* q, int* token, float* va, float* vb) {
+__device__ __forceinline__ void reduce_item(const float4* red, int i, int* q, int* token, float* va, float* vb,
+                                            int ns = 1) {
   const int nt = i >> 6, j = i & 63, lane = j >> 1, which = j & 1;
   *q = lane >> 2;
   *token = 8 * nt + 2 * (lane & 3) + which;
-  const float* r0 = reinterpret_cast<const float*>(&red[nt * 32 + lane]);
-  float a = r0[which], b = r0[which + 2];
+  float A = 0.f, B = 0.f;
+  for (int s = 0; s < ns; s++) {
+    const float4* rs = red + s * WARPS * NT * 32;
+    const float* r0 = reinterpret_cast<const float*>(&rs[nt * 32 + lane]);
+    float a = r0[which], b = r0[which + 2];
 #pragma unroll
-  for (int w = 1; w < WARPS; w++) {
-    const float* r = reinterpret_cast<const float*>(&red[(w * NT + nt) * 32 + lane]);
-    a = __fadd_rn(a, r[which]);
-    b = __fadd_rn(b, r[which + 2]);
+    for (int w = 1; w < WARPS; w++) {
+      const float* r = reinterpret_cast<const float*>(&rs[(w * NT + nt) * 32 + lane]);
+      a = __fadd_rn(a, r[which]);
+      b = __fadd_rn(b, r[which + 2]);
+    }
+    A = s == 0 ? a : __fadd_rn(A, a);
+    B = s == 0 ? b : __fadd_rn(B, b);
   }
-  *va = a;
-  *vb = b;
+  *va = A;
+  *vb = B;
 }
 
 // Virtual row `a` of epi_pair (epilogue.cuh) for pair q of tile j.
