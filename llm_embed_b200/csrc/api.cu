@@ -153,6 +153,7 @@ struct Layer {
 struct Workspace {
   int cap_tokens = 0, cap_seqs = 0;
   DevBuf ids, offsets, pos, h32, y32, hA, qkv, att, ff, out;
+  DevBuf att_units;  // the short-sequence attention's work list
   DevBuf ln_part, ln_ctl;  // row statistics of the fused projection + LayerNorm
   HostBuf h_ids, h_offsets, h_out;
 };
@@ -402,6 +403,7 @@ static int ensure_ws(le_model* m, int tokens, int seqs) {
   if (seqs > w.cap_seqs) {
     const size_t S = (size_t)std::max(seqs, 64);
     TRY(w.offsets.ensure((S + 1) * 4));
+    TRY(w.att_units.ensure(attention_units_bytes((int)S)));
     TRY(w.out.ensure(S * H * 4));
     TRY(w.h_offsets.ensure((S + 1) * 4));
     TRY(w.h_out.ensure(S * H * 4));
@@ -527,6 +529,12 @@ static int forward(le_model* m, const int32_t* d_ids, const int32_t* d_offsets, 
     // Large batches: the out and down projections carry the residual add
     // and LayerNorm in their epilogue (same bits as GEMM + launch_ln_add).
     const bool fuse_ln = T >= TC_F16_MIN_M && gemm_ln_supported(H, H) && gemm_ln_supported(H, F);
+    // Batches whose GEMMs run on tensor cores also run the short
+    // sequences' attention on them (its work list built here, once); small
+    // batches keep the mma.sync tile (the same bits as the single-kernel
+    // forward).
+    const bool att_tc = T >= TC_MIN_M && m->head_dim == 64;
+    if (att_tc) PLAUNCH(7, launch_attention_units(d_offsets, nseq, w.cap_seqs, w.att_units.p, s));
     for (const Layer& L : m->layers) {
       EpiParams e{};
       e.M = T;
@@ -540,11 +548,9 @@ static int forward(le_model* m, const int32_t* d_ids, const int32_t* d_offsets, 
       e.head_dim = m->head_dim;
       e.rope_cols = 2 * H;
       TRY(gemm(m, 0, L.qkv, hA, H, e, s));
-      // Batches whose GEMMs run on tensor cores also run the short
-      // sequences' attention on them; small batches keep the mma.sync tile
-      // (the same bits as the single-kernel forward).
-      if (T >= TC_MIN_M && m->head_dim == 64)
-        PLAUNCH(4, launch_attention_stc(qkv, d_offsets, nseq, T, H, m->hp.heads, att, m->status.as<DevStatus>(), s));
+      if (att_tc)
+        PLAUNCH(4, launch_attention_stc(qkv, w.att_units.p, w.cap_seqs, nseq, T, H, m->hp.heads, att,
+                                        m->status.as<DevStatus>(), s));
       else
         PLAUNCH(4, launch_attention(qkv, d_offsets, nseq, max_len, H, m->hp.heads, m->head_dim, att, s));
       if (max_len > ATTN_SHORT_MAX)

@@ -4,23 +4,33 @@
 //
 // Persistent kernel, one CTA per SM, four independent groups of four warps
 // (thread = query row = TMEM lane), each with a unit in flight in its own
-// 128-column TMEM slot.  A unit's whole key range fits one MMA: S = Q.K^T
-// (M=128 query rows, N=L rounded up to 16, K=64) into the slot; the group
-// reads its rows of S, finds the exact maximum and writes P = exp(0.125 S -
-// max) (0 when more than 10 below the maximum, the reference's rule,
-// ops_simd.go:70-82) as fp16 pairs back into the slot over the scores it has
-// read; O = P.V (A = P from TMEM, B = V from shared memory; N=64, K=L
-// rounded up to 16) lands in the slot's upper 64 columns, and the group
-// normalises and stores it.  Warps whose 32 rows all lie past the sequence
+// 128-column TMEM slot.  A unit is one head of one sequence of 65..128
+// tokens, or of two sequences of at most 64 tokens packed into query rows
+// 0..63 (A) and 64..127 (B); the work list comes from attention_units_kernel
+// (below), once per forward.  A unit's whole key range fits one MMA: S =
+// Q.K^T (M=128 query rows, N = the keys rounded up to 16: 128 when packed,
+// A's keys in columns 0..63 and B's in 64..127, K=64) into the slot; each
+// row reads its own sequence's scores, finds the exact maximum and writes P
+// = exp(0.125 S - max) (0 when more than 10 below the maximum, the
+// reference's rule, ops_simd.go:70-82) as fp16 pairs back into the slot
+// over the scores it has read, and zeros over the other sequence's keys;
+// O = P.V (A = P from TMEM, B = V from shared memory; N=64, K = the keys)
+// lands in the slot's upper 64 columns, and the group normalises and stores
+// it.  A row's scores, P and O are those of the same row in a unit of its
+// sequence alone (the other sequence's keys add exact zeros), so packing
+// does not change any bit.  Warps whose 32 rows all lie past their sequence
 // skip the unit's arithmetic.
 //
 // One elected thread per group (lane 0 of its first warp) takes the CTA's
-// next unit from a shared counter and issues everything asynchronous of the
-// group: the TMA loads of the next unit's Q|K (as soon as S has read the
-// current ones) and V (as soon as P.V has read the current ones), S of the
-// next unit (once the group has read O out of the slot), and P.V.  The four
-// warps meet at two named barriers per unit (P written; O read).  No group
-// ever waits for another, so a long unit holds back only its own group.
+// next unit from a shared counter (unit u = descriptor u / heads, head u %
+// heads; CTA c takes c, c + grid, ... in turn) and issues everything
+// asynchronous of the group: the TMA loads of the next unit's Q|K (as soon
+// as S has read the current ones) and V (once the group has staged its
+// output through the V buffer), S of the next unit (once the group has read
+// O out of the slot), and P.V.  The four warps meet at two named barriers
+// per unit (P written; O read), and the elected thread's warp waits for the
+// others at a third (V buffer free).  No group ever waits for another, so a
+// long unit holds back only its own group.
 //
 // Operands: one TMA map over qkv [T][3H] (64-column boxes of 64 rows,
 // 128-byte swizzle); Q and K K-major; V [keys][64] the MN-major B operand of
@@ -63,10 +73,23 @@ struct Lay {
   static constexpr int NBAR = 4 * G;
   static constexpr int OFF_MISC = OFF_BAR + NBAR * 8;  // abort flag, TMEM base, unit counter
   static constexpr int OFF_UNITS = OFF_MISC + 16;      // next unit [G][2] (int4)
-  static constexpr int BYTES = OFF_UNITS + 16 * 2 * G;
+  static constexpr int OFF_GS = OFF_UNITS + 16 * 2 * G;  // GroupState [G]
+  static constexpr int BYTES = OFF_GS + 80 * G;
   static constexpr int ALLOC = BYTES + 1024;
   static_assert(ALLOC <= 232448, "shared memory budget");
 };
+
+// The elected thread's bookkeeping, kept in shared memory so that the
+// registers go to the rows' scores: the unit whose Q|K are loading, the
+// unit fetch in flight, and the phases issued / waited (for the drain on
+// exit).
+struct GroupState {
+  int4 un;
+  int4 desc;     // the fetched unit's descriptor (cp.async target)
+  long long pu;  // counter value taken (-1: none in flight)
+  uint32_t nq, nqw, nv, nvw, ns, no, sw, ow;
+};
+static_assert(sizeof(GroupState) <= 80, "group state slot");
 
 __device__ __forceinline__ void tmem_ld32_nowait(uint32_t taddr, uint32_t* r) {
   asm volatile(
@@ -184,15 +207,75 @@ __device__ __forceinline__ void mma_f16_ts(uint32_t tmem_d, uint32_t tmem_a, uin
       "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n}\n" ::"r"(tmem_d),
       "r"(tmem_a), "l"(bdesc), "r"(idesc), "r"(accumulate));
 }
-// Unit u -> (sequence, head); its length (0 when the unit is not this
-// kernel's: empty or longer than MAXL).
-__device__ __forceinline__ int unit_len(const int32_t* offsets, int heads, int u, int* t0, int* head) {
-  const int s = u / heads;
-  *head = u - s * heads;
-  *t0 = offsets[s];
-  const int L = offsets[s + 1] - *t0;
-  return L > MAXL ? 0 : L;
+// ---------------------------------------------------------------- unit list
+//
+// The kernel's work list, built once per forward: descriptors {t0A, LA,
+// t0B, LB} (LB = 0: one sequence), each taken by `heads` units.  A sequence
+// of PACK_MAX + 1 .. MAXL tokens is one descriptor; sequences of at most
+// PACK_MAX tokens go two to a descriptor (a lone last one alone).
+// Descriptors are ordered longest first (sequences sorted by length; the
+// short ones paired in that order), so the units every CTA takes in turn
+// are of about the same length and the CTAs finish together.  Empty
+// sequences and those longer than MAXL (attention_tc.cu) are left out.
+//
+// Buffer: descriptors [cap] int4, sorted sequence indices [cap] int32, then
+// the descriptor count (int32, 16-byte aligned).
+constexpr int PACK_MAX = 64;
+__host__ __device__ inline size_t units_sorted_off(int cap) { return (size_t)cap * 16; }
+__host__ __device__ inline size_t units_count_off(int cap) { return ((size_t)cap * 20 + 15) & ~(size_t)15; }
+
+// One CTA: a counting sort of the sequences by length (descending), then
+// the descriptors.  The order of equal lengths follows the atomics; a row's
+// result does not depend on the sequence it is packed with.
+__global__ void __launch_bounds__(1024) attention_units_kernel(const int32_t* __restrict__ offsets, int nseq, int cap,
+                                                               uint8_t* __restrict__ buf) {
+  int4* desc = reinterpret_cast<int4*>(buf);
+  int32_t* sorted = reinterpret_cast<int32_t*>(buf + units_sorted_off(cap));
+  int32_t* count = reinterpret_cast<int32_t*>(buf + units_count_off(cap));
+  __shared__ int hist[MAXL + 1], next[MAXL + 1], totals[2];
+  for (int i = threadIdx.x; i <= MAXL; i += blockDim.x) hist[i] = 0;
+  __syncthreads();
+  for (int q = threadIdx.x; q < nseq; q += blockDim.x) {
+    const int L = offsets[q + 1] - offsets[q];
+    if (L >= 1 && L <= MAXL) atomicAdd(&hist[L], 1);
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    int acc = 0;
+    for (int L = MAXL; L >= 1; L--) {
+      next[L] = acc;
+      acc += hist[L];
+      if (L == PACK_MAX + 1) totals[0] = acc;
+    }
+    totals[1] = acc;
+    *count = totals[0] + (acc - totals[0] + 1) / 2;
+  }
+  __syncthreads();
+  for (int q = threadIdx.x; q < nseq; q += blockDim.x) {
+    const int L = offsets[q + 1] - offsets[q];
+    if (L >= 1 && L <= MAXL) sorted[atomicAdd(&next[L], 1)] = q;
+  }
+  __syncthreads();
+  const int nlong = totals[0], nall = totals[1];
+  const int ndesc = nlong + (nall - nlong + 1) / 2;
+  for (int d = threadIdx.x; d < ndesc; d += blockDim.x) {
+    const int j = d < nlong ? d : nlong + 2 * (d - nlong);
+    const int a = sorted[j];
+    int4 v = make_int4(offsets[a], offsets[a + 1] - offsets[a], 0, 0);
+    if (d >= nlong && j + 1 < nall) {
+      const int b = sorted[j + 1];
+      v.z = offsets[b];
+      v.w = offsets[b + 1] - offsets[b];
+    }
+    desc[d] = v;
+  }
 }
+
+// A unit in flight as {t0A, LA | head << 8, t0B, LB} (LA = 0: none).
+__device__ __forceinline__ int unit_la(int4 u) { return u.y & 0xFF; }
+__device__ __forceinline__ int unit_head(int4 u) { return u.y >> 8; }
+// S's N and P.V's K: every key column of the unit, rounded up to 16.
+__device__ __forceinline__ int unit_np(int4 u) { return u.w > 0 ? 2 * PACK_MAX : (unit_la(u) + 15) & ~15; }
 
 // OR of `v` over the 128 threads of named barrier `id` (all of them get
 // the same answer), with the barrier's memory ordering.
@@ -216,8 +299,9 @@ __device__ __forceinline__ void drain(uint32_t bar, uint32_t parity) {
 
 // 128 registers per thread: 16 warps of 32 threads share the SM's 64K.
 __global__ void __launch_bounds__(NTHREADS, 1)
-    attention_stc_kernel(const __grid_constant__ CUtensorMap tmap, const int32_t* __restrict__ offsets, int nunits,
-                         int heads, int H, __half* __restrict__ out, DevStatus* status) {
+    attention_stc_kernel(const __grid_constant__ CUtensorMap tmap, const int4* __restrict__ desc,
+                         const int32_t* __restrict__ desc_count, int heads, int H, __half* __restrict__ out,
+                         DevStatus* status) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
   const uint32_t sbase = smem_u32(smem);
@@ -247,8 +331,6 @@ __global__ void __launch_bounds__(NTHREADS, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  pdl_wait();  // qkv and the output buffer are the previous kernels'
-  pdl_trigger();
 
   const int quarter = warp & 3;         // TMEM lanes 32*quarter .. +31
   const int row = quarter * 32 + lane;  // query row of the unit
@@ -258,29 +340,55 @@ __global__ void __launch_bounds__(NTHREADS, 1)
   const uint32_t col = tmem + grp * MAXL;  // the group's slot
   const uint32_t slot = col + ((uint32_t)(quarter * 32) << 16);
 
-  // A unit as {first token, head, length} (length 0: none).  Elected
-  // thread: the CTA's next unit with work for this kernel.
+  // The descriptor list was written before the previous kernel started (a
+  // forward builds it before its first layer), so it is read before the
+  // wait on the previous kernel.
+  const long long nunits = (long long)__ldg(desc_count) * heads;
+  auto unit_of = [&](long long u, int4 d) { return make_int4(d.x, d.y | ((int)(u % heads) << 8), d.z, d.w); };
+  // Elected thread: the CTA's next unit.
   auto fetch = [&]() -> int4 {
-    for (;;) {
-      const long u = blockIdx.x + (long)atomicAdd(unit_ctr, 1) * gridDim.x;
-      if (u >= nunits) return make_int4(0, 0, 0, 0);
-      int t0, head;
-      const int L = unit_len(offsets, heads, (int)u, &t0, &head);
-      if (L > 0) return make_int4(t0, head, L, 0);
-    }
+    const long long u = blockIdx.x + (long long)atomicAdd(unit_ctr, 1) * gridDim.x;
+    if (u >= nunits) return make_int4(0, 0, 0, 0);
+    return unit_of(u, __ldg(desc + u / heads));
   };
+  // The same in two steps, so that the descriptor load is in flight while
+  // the group works: fetch_issue takes the counter and copies the
+  // descriptor to shared memory (cp.async), fetch_resolve (a phase later)
+  // waits for the copy.
+  GroupState& gs = *reinterpret_cast<GroupState*>(smem + Lay::OFF_GS + 80 * grp);
+  auto fetch_issue = [&]() {
+    const long long u = blockIdx.x + (long long)atomicAdd(unit_ctr, 1) * gridDim.x;
+    gs.pu = u;
+    if (u < nunits)
+      asm volatile("cp.async.ca.shared.global [%0], [%1], 16;\n" ::"r"(smem_u32(&gs.desc)), "l"(desc + u / heads)
+                   : "memory");
+  };
+  auto fetch_resolve = [&]() -> int4 {
+    const long long u = gs.pu;
+    gs.pu = -1;
+    if (u < 0 || u >= nunits) return make_int4(0, 0, 0, 0);
+    asm volatile("cp.async.wait_all;\n" ::: "memory");
+    return unit_of(u, gs.desc);
+  };
+  // Rows 0..63 of Q, K and V from A's first token, rows 64..127 from B's
+  // (packed) or A's 65th (K and V only when A has more than 64 tokens).
+  auto nbox_of = [&](int4 un) { return un.w > 0 ? 2 : (unit_la(un) + BOX - 1) / BOX; };
+  auto box1_of = [&](int4 un) { return un.w > 0 ? un.z : un.x + BOX; };
   auto load_qk = [&](int4 un) {
-    const int nbox = (un.z + BOX - 1) / BOX;
+    const int nbox = nbox_of(un), c = unit_head(un) * HD, r1 = box1_of(un);
     mbar_expect_tx(qk_full, QKV_BYTES + nbox * BOX * HD * 2);
-    for (int x = 0; x < 2; x++) tma_load_2d(sq + x * BOX * 128, &tmap, un.y * HD, un.x + x * BOX, qk_full);
-    for (int x = 0; x < nbox; x++) tma_load_2d(sk + x * BOX * 128, &tmap, H + un.y * HD, un.x + x * BOX, qk_full);
+    tma_load_2d(sq, &tmap, c, un.x, qk_full);
+    tma_load_2d(sq + BOX * 128, &tmap, c, r1, qk_full);
+    tma_load_2d(sk, &tmap, H + c, un.x, qk_full);
+    if (nbox > 1) tma_load_2d(sk + BOX * 128, &tmap, H + c, r1, qk_full);
   };
   auto load_v = [&](int4 un) {
-    const int nbox = (un.z + BOX - 1) / BOX;
+    const int nbox = nbox_of(un), c = 2 * H + unit_head(un) * HD;
     mbar_expect_tx(v_full, nbox * BOX * HD * 2);
-    for (int x = 0; x < nbox; x++) tma_load_2d(sv + x * BOX * 128, &tmap, 2 * H + un.y * HD, un.x + x * BOX, v_full);
+    tma_load_2d(sv, &tmap, c, un.x, v_full);
+    if (nbox > 1) tma_load_2d(sv + BOX * 128, &tmap, c, box1_of(un), v_full);
   };
-  // S = Q . K^T into the slot (N = L rounded up to 16).
+  // S = Q . K^T into the slot (N = the unit's keys rounded up to 16).
   auto issue_s = [&](int np) {
     const uint32_t idesc = idesc_f16(BQ, np);
 #pragma unroll
@@ -288,7 +396,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
       mma_f16(col, sw128_desc(sq + kk * 32), sw128_desc(sk + kk * 32), idesc, kk != 0);
     mma_commit(s_full);
   };
-  // O = P.V, P read from the slot's TMEM (K = L rounded up to 16).
+  // O = P.V, P read from the slot's TMEM (K = the unit's keys).
   auto issue_pv = [&](int np) {
     const uint32_t idesc = idesc_f16(BQ, HD) | (1u << 16);  // B (V) MN-major
     for (int kk = 0; kk < np / 16; kk++)
@@ -296,48 +404,57 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     mma_commit(o_full);
   };
 
-  // Phases issued / waited by the elected thread (for the drain on exit).
-  uint32_t nq = 0, nqw = 0, nv = 0, nvw = 0, ns = 0, no = 0;
   bool bad = false;
-  // Elected thread: the unit after the one in flight, taken a unit ahead so
-  // that the counter and offsets loads stay off the group's critical path.
-  int4 ua = make_int4(0, 0, 0, 0);
+  // The first units are taken before the wait on the previous kernel (which
+  // wrote qkv).
+  int4 u0 = make_int4(0, 0, 0, 0);
   if (elect) {
+    gs.un = make_int4(0, 0, 0, 0);
+    gs.pu = -1;
+    gs.nq = gs.nqw = gs.nv = gs.nvw = gs.ns = gs.no = gs.sw = gs.ow = 0;
     asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmap)) : "memory");
-    const int4 u0 = fetch();
+    u0 = fetch();
     unit_next[0] = u0;
-    if (u0.z > 0) {
-      ua = fetch();
-      load_qk(u0), nq++;
-      load_v(u0), nv++;
+    if (unit_la(u0) > 0) fetch_issue();
+  }
+  pdl_wait();  // qkv and the output buffer are the previous kernels'
+  pdl_trigger();
+  if (elect) {
+    if (unit_la(u0) > 0) {
+      load_qk(u0), gs.nq++;
+      load_v(u0), gs.nv++;
       bad = !mbar_wait_sleep(qk_full, 0, abort_flag, status, 81);
-      if (!bad) nqw++, issue_s((u0.z + 15) & ~15), ns++;
+      if (!bad) gs.nqw++, issue_s(unit_np(u0)), gs.ns++;
     }
   }
   bad = group_any(bar_id, bad);
   int4 cur = bad ? make_int4(0, 0, 0, 0) : unit_next[0];
-  uint32_t sw = 0, ow = 0;  // phases of s_full / o_full the elected thread saw
-  for (int k = 0; cur.z > 0; k++) {
-    const int t0 = cur.x, head = cur.y, L = cur.z;
-    const int np = (L + 15) & ~15;
-    // A warp whose 32 rows are all past the sequence has nothing to do:
+  for (int k = 0; unit_la(cur) > 0; k++) {
+    const int head = unit_head(cur), np = unit_np(cur);
+    const bool packed = cur.w > 0;
+    // This warp's rows: of B (rows 64..127 of a packed unit) or of A.
+    const int rbase = packed && quarter >= 2 ? PACK_MAX : 0;
+    const int t0 = rbase ? cur.z : cur.x, L = rbase ? cur.w : unit_la(cur);
+    const uint32_t srow = slot + rbase;      // the row's keys in S
+    const uint32_t prow = slot + rbase / 2;  // and their P pairs
+    // A warp whose 32 rows are all past its sequence has nothing to do:
     // its rows of P and O are never stored (rows are independent in both
     // MMAs).
-    const bool live = quarter * 32 < L;
+    const bool live = quarter * 32 - rbase < L;
     // (Only the elected thread can come here with `bad` set: a failed wait
     // after the last barrier.  Its warp then fails as a whole.)
     if (live || elect) {
       const bool w = !bad && mbar_wait(s_full, k & 1, abort_flag, status, 87);
       bad = !__all_sync(0xffffffffu, w);
-      if (elect && !bad) sw++;
+      if (elect && !bad) gs.sw++;
     }
     tc_fence_after();
-    int4 un = make_int4(0, 0, 0, 0);
     if (elect && !bad) {
       // Q and K are read: the next unit's go to the same buffers.
-      un = ua;
+      const int4 un = fetch_resolve();
+      gs.un = un;
       unit_next[(k + 1) & 1] = un;
-      if (un.z > 0) load_qk(un), nq++;
+      if (unit_la(un) > 0) load_qk(un), gs.nq++;
     }
     float l = 0.f;
     if (live && !bad) {
@@ -347,36 +464,46 @@ __global__ void __launch_bounds__(NTHREADS, 1)
       float m0 = -INFINITY, m1 = -INFINITY;
       {
         uint32_t ra[16], rb[16];
-        tmem_ld16_nowait(slot, ra);
+        tmem_ld16_nowait(srow, ra);
 #pragma unroll
         for (int c = 0; c < MAXL / 16; c += 2) {
           if (c < n16) {
             tmem_wait_ld();
-            if (c + 1 < n16) tmem_ld16_nowait(slot + (c + 1) * 16, rb);
+            if (c + 1 < n16) tmem_ld16_nowait(srow + (c + 1) * 16, rb);
             chunk_max<16>(m0, m1, ra, L - c * 16);
           }
           if (c + 1 < n16) {
             tmem_wait_ld();
-            if (c + 2 < n16) tmem_ld16_nowait(slot + (c + 2) * 16, ra);
+            if (c + 2 < n16) tmem_ld16_nowait(srow + (c + 2) * 16, ra);
             chunk_max<16>(m0, m1, rb, L - (c + 1) * 16);
           }
         }
       }
       const float mx = fmaxf(m0, m1);
       // P, PK keys per TMEM load, over the scores already read: keys PK c ..
-      // to columns PK/2 c ..
-      // (columns past the unit's N hold no scores of it: masked, and P.V
-      // reads only the first L/2 rounded up to 8).
+      // to columns PK/2 c .. (columns past the unit's N hold no scores of
+      // it: masked, and P.V reads only the first N/2).
       const unsigned long long scale = f2_pack(SCALE2, SCALE2), off = f2_pack(-mx * SCALE2, -mx * SCALE2);
       unsigned long long s0 = f2_pack(0.f, 0.f), s1 = s0;
       const int nst = (L + PK - 1) / PK;
 #pragma unroll 1
       for (int c = 0; c < nst; c++) {
         uint32_t r[PK], w[PK / 2];
-        tmem_ld_nowait<PK>(slot + c * PK, r);
+        tmem_ld_nowait<PK>(srow + c * PK, r);
         tmem_wait_ld();
         chunk_p<PK>(r, L - c * PK, scale, off, s0, s1, w);
-        tmem_st_half<PK>(slot + c * (PK / 2), w);
+        tmem_st_half<PK>(prow + c * (PK / 2), w);
+      }
+      if (packed) {
+        // P.V reads all 64 pair columns: zeros over the other sequence's
+        // keys and over this one's past its last 16-key step (written after
+        // the scores there have been read).
+        const uint32_t z[8] = {0u, 0u, 0u, 0u, 0u, 0u, 0u, 0u};
+#pragma unroll 1
+        for (int c = 0; c < 2 * PACK_MAX / 16; c++) {
+          const int c8 = c * 8;
+          if (c8 < rbase / 2 || c8 >= rbase / 2 + nst * (PK / 2)) tmem_st8(slot + c8, z);
+        }
       }
       float l0, l1;
       f2_unpack(f2_add(s0, s1), l0, l1);
@@ -388,17 +515,15 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     if (elect) {
       tc_fence_after();
       bad = !mbar_wait_sleep(v_full, k & 1, abort_flag, status, 84);
-      if (!bad) nvw++, issue_pv(np), no++;
-      ua = un.z > 0 ? fetch() : make_int4(0, 0, 0, 0);
+      if (!bad) gs.nvw++, issue_pv(np), gs.no++;
+      if (unit_la(gs.un) > 0) fetch_issue();
     }
     if (live || elect) {
       const bool w = !bad && mbar_wait(o_full, k & 1, abort_flag, status, 88);
       bad = !__all_sync(0xffffffffu, w);
-      if (elect && !bad) ow++;
+      if (elect && !bad) gs.ow++;
     }
     tc_fence_after();
-    // V is read: the next unit's goes to the same buffer.
-    if (elect && !bad && un.z > 0) load_v(un), nv++;
     uint32_t o[64];
     if (live && !bad) {
       tmem_ld32_nowait(slot + TM_O, o);
@@ -408,16 +533,21 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     tc_fence_before();
     if (group_any(bar_id, bad)) break;  // O is read: the slot is free
     cur = unit_next[(k + 1) & 1];
-    if (elect && cur.z > 0) {
+    if (elect && unit_la(cur) > 0) {
       // S of the next unit, overlapping this unit's stores.
       tc_fence_after();
       bad = !mbar_wait_sleep(qk_full, (k + 1) & 1, abort_flag, status, 81);
-      if (!bad) nqw++, issue_s((cur.z + 15) & ~15), ns++;
+      if (!bad) gs.nqw++, issue_s(unit_np(cur)), gs.ns++;
     }
-    if (live && !bad && row < L) {
+    if (live && !bad) {
+      // O / l as fp16 through shared memory (the V buffer: P.V has read
+      // it), so that the global stores are whole 128-byte row segments:
+      // the warp writes its 32 rows (16-byte chunks swizzled by row) and
+      // reads them back four rows per instruction.  Rows past the sequence
+      // (l may be 0 there) are staged but never stored.
+      uint8_t* stg = smem + grp * Lay::GSTRIDE + 2 * QKV_BYTES + quarter * 32 * 128;
       const float inv = 1.0f / l;
       const unsigned long long inv2 = f2_pack(inv, inv);
-      uint4* dst = reinterpret_cast<uint4*>(out + (long)(t0 + row) * H + head * HD);
 #pragma unroll
       for (int c = 0; c < 8; c++) {
         uint32_t h[4];
@@ -428,17 +558,35 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                     b);
           h[j] = pack_half2(a, b);
         }
-        dst[c] = make_uint4(h[0], h[1], h[2], h[3]);
+        *reinterpret_cast<uint4*>(stg + lane * 128 + ((c ^ (lane & 7)) << 4)) = make_uint4(h[0], h[1], h[2], h[3]);
+      }
+      __syncwarp();
+      const int c = lane & 7;
+#pragma unroll
+      for (int i = 0; i < 8; i++) {
+        const int r = 4 * i + (lane >> 3);        // the warp's row
+        const int rr = quarter * 32 + r - rbase;  // the row in its sequence
+        const uint4 v = *reinterpret_cast<const uint4*>(stg + r * 128 + ((c ^ (r & 7)) << 4));
+        if (rr < L) reinterpret_cast<uint4*>(out + (long)(t0 + rr) * H + head * HD)[c] = v;
       }
     }
+    // The V buffer is free once every warp has read its rows back: the
+    // elected thread's warp waits for the others at a named barrier, then
+    // the next unit's V goes to the buffer.
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    if (quarter == 0)
+      asm volatile("bar.sync %0, 128;" ::"r"(bar_id + G) : "memory");
+    else
+      asm volatile("bar.arrive %0, 128;" ::"r"(bar_id + G) : "memory");
+    if (elect && !bad && unit_la(gs.un) > 0) load_v(gs.un), gs.nv++;
   }
   // Copies and MMAs this group's elected thread issued but nobody waited
   // for (only after a failure) land before the CTA exits.
   if (elect) {
-    if (nq > nqw) drain(qk_full, (nq - 1) & 1);
-    if (nv > nvw) drain(v_full, (nv - 1) & 1);
-    if (ns > sw) drain(s_full, (ns - 1) & 1);
-    if (no > ow) drain(o_full, (no - 1) & 1);
+    if (gs.nq > gs.nqw) drain(qk_full, (gs.nq - 1) & 1);
+    if (gs.nv > gs.nvw) drain(v_full, (gs.nv - 1) & 1);
+    if (gs.ns > gs.sw) drain(s_full, (gs.ns - 1) & 1);
+    if (gs.no > gs.ow) drain(o_full, (gs.no - 1) & 1);
   }
 
   tc_fence_before();
@@ -464,13 +612,23 @@ static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
 
 }  // namespace stc
 
-cudaError_t launch_attention_stc(const __half* qkv, const int32_t* offsets, int nseq, int T, int H, int heads,
+size_t attention_units_bytes(int cap) { return stc::units_count_off(cap) + 16; }
+
+cudaError_t launch_attention_units(const int32_t* offsets, int nseq, int cap, void* buf, cudaStream_t s) {
+  if (nseq <= 0) return cudaSuccess;
+  if (nseq > cap || !buf || (reinterpret_cast<uintptr_t>(buf) & 15)) return cudaErrorInvalidValue;
+  stc::attention_units_kernel<<<1, 1024, 0, s>>>(offsets, nseq, cap, static_cast<uint8_t*>(buf));
+  return cudaGetLastError();
+}
+
+cudaError_t launch_attention_stc(const __half* qkv, const void* units, int cap, int nseq, int T, int H, int heads,
                                  __half* out, DevStatus* status, cudaStream_t s) {
   if (nseq == 0 || T == 0) return cudaSuccess;
-  if (H != heads * stc::HD) return cudaErrorInvalidValue;
+  if (H != heads * stc::HD || heads >= (1 << 22) || nseq > cap) return cudaErrorInvalidValue;
   auto enc = stc::encode_fn();
   if (!enc) return cudaErrorNotSupported;
-  if ((3L * H * 2) % 16 || (reinterpret_cast<uintptr_t>(qkv) & 15)) return cudaErrorInvalidValue;
+  if ((3L * H * 2) % 16 || (reinterpret_cast<uintptr_t>(qkv) & 15) || (reinterpret_cast<uintptr_t>(units) & 15))
+    return cudaErrorInvalidValue;
   CUtensorMap map;
   const cuuint64_t dims[2] = {(cuuint64_t)(3 * H), (cuuint64_t)T};
   const cuuint64_t strides[1] = {(cuuint64_t)(3 * H) * 2};
@@ -494,12 +652,14 @@ cudaError_t launch_attention_stc(const __half* qkv, const int32_t* offsets, int 
       cudaDeviceGetAttribute(&sms[dev], cudaDevAttrMultiProcessorCount, dev);
     }
   }
+  // At most nseq * heads units (fewer when sequences are packed).
   const long nunits = (long)nseq * heads;
-  if (nunits > 0x7fffffff) return cudaErrorInvalidValue;
   const int grid = nunits < sms[dev] ? (int)nunits : sms[dev];
+  const uint8_t* ub = static_cast<const uint8_t*>(units);
   cudaLaunchAttribute attr[1];
   const cudaLaunchConfig_t cfg = pdl_config(dim3(grid), dim3(stc::NTHREADS), stc::Lay::ALLOC, s, attr);
-  return cudaLaunchKernelEx(&cfg, stc::attention_stc_kernel, map, offsets, (int)nunits, heads, H, out, status);
+  return cudaLaunchKernelEx(&cfg, stc::attention_stc_kernel, map, reinterpret_cast<const int4*>(ub),
+                            reinterpret_cast<const int32_t*>(ub + stc::units_count_off(cap)), heads, H, out, status);
 }
 
 }  // namespace le

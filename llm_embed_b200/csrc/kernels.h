@@ -36,8 +36,12 @@ constexpr int ATTN_SHORT_MAX = 128;
 cudaError_t launch_attention(const __half* qkv, const int32_t* offsets, int nseq, int max_len, int H, int heads,
                              int head_dim, __half* out, cudaStream_t s);
 // attention_stc.cu: sequences of at most ATTN_SHORT_MAX tokens in large
-// batches (persistent tcgen05 kernel over (sequence, head) units).
-cudaError_t launch_attention_stc(const __half* qkv, const int32_t* offsets, int nseq, int T, int H, int heads,
+// batches (persistent tcgen05 kernel over (sequences, head) units).  The
+// unit list (attention_units_bytes(cap) bytes, cap >= nseq) is built once
+// per forward by launch_attention_units, before the layers.
+size_t attention_units_bytes(int cap);
+cudaError_t launch_attention_units(const int32_t* offsets, int nseq, int cap, void* buf, cudaStream_t s);
+cudaError_t launch_attention_stc(const __half* qkv, const void* units, int cap, int nseq, int T, int H, int heads,
                                  __half* out, DevStatus* status, cudaStream_t s);
 // attention_tc.cu: sequences of at least min_len tokens (tcgen05), T = rows of qkv
 cudaError_t launch_attention_tc(const __half* qkv, const int32_t* offsets, int nseq, int T, int max_len, int min_len,
