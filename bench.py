@@ -348,11 +348,16 @@ class Ctx:
         return [a.elapsed_time(c) for a, c in ev], launches, clk
 
     def profile(self, b, steps):
-        """Per-class device time from a pass with events around every launch."""
+        """Per-class device time from a pass with events around every launch.
+        A spin kernel ahead of each step keeps the GPU busy while the host
+        enqueues the step, so an event pair times the kernel between them,
+        not the host's launch work (kernels still run one after another:
+        no programmatic overlap between them in this pass)."""
         torch = self.torch
         b.e.set_profiling(True)
         for _ in range(steps):
             self.flush.zero_()
+            torch.cuda._sleep(4_000_000 * len(b.calls))  # ~2 ms per device call at ~2 GHz
             b.step()
         torch.cuda.synchronize()
         st = b.e.stats(reset=True)
@@ -469,6 +474,9 @@ def latency(ctx, e, res):
     for i in range(60):
         a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         ctx.flush.zero_()
+        # The GPU spins while the host enqueues the call, so the events
+        # time the forward on the device, not the host's launch work.
+        torch.cuda._sleep(2_000_000)
         a.record(ctx.stream)
         e.embed_device(d_ids.data_ptr(), d_offs.data_ptr(), 1, 8, 8, d_out.data_ptr(), ctx.stream.cuda_stream)
         b.record(ctx.stream)
