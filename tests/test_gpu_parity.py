@@ -182,6 +182,44 @@ def test_attention_length_classes(model_path, lens):
     assert_parity(got, ref)
 
 
+def test_short_attention_packing_is_invisible(model_path):
+    """The tensor-core short attention packs sequences of at most 64 tokens
+    two to a 128-row unit, paired in length order, and runs the units
+    longest first.  A sequence's embedding must not depend on its partner:
+    the same short sequences in three batches that pair them differently
+    (another order, one more short sequence shifting every pair, a lone
+    short one left unpaired) give the same bits, and match the oracle."""
+    spec = small_spec(context=512)
+    path = model_path(spec)
+    shorts = [64, 64, 63, 33, 32, 17, 16, 9, 2, 1, 48]
+    longs = [65, 128, 129, 97]
+    lens = shorts + longs  # 11 short: one left alone
+    ids, offs = synth.make_ids(lens, seed=31, vocab=spec.vocab)
+    seqs = [ids[offs[i]:offs[i + 1]] for i in range(len(lens))]
+
+    def batch(order, extra=()):
+        parts = [seqs[i] for i in order] + list(extra)
+        o = np.concatenate([[0], np.cumsum([len(p) for p in parts])]).astype(np.int32)
+        return np.concatenate(parts).astype(np.int32), o
+
+    e = Embedder.Load(path)
+    try:
+        got = e.EmbedIDs(ids, offs)
+        order = list(range(len(lens)))[::-1]
+        b_ids, b_offs = batch(order)
+        rev = e.EmbedIDs(b_ids, b_offs)
+        extra = synth.make_ids([40], seed=32, vocab=spec.vocab)[0]
+        c_ids, c_offs = batch(range(len(lens)), [extra])  # 12 short: pairs shift
+        more = e.EmbedIDs(c_ids, c_offs)
+    finally:
+        e.Close()
+    assert offs[-1] >= 64  # the tensor-core attention path
+    for k, i in enumerate(order):
+        assert np.array_equal(rev[k].view(np.uint32), got[i].view(np.uint32)), f"reversed, sequence {i}"
+    assert np.array_equal(more[:len(lens)].view(np.uint32), got.view(np.uint32))
+    assert_parity(got, _oracle_embed(path, ids, offs), tag="short attention packing")
+
+
 def test_context_length_enforced(model_path):
     spec = small_spec(context=512, seed=12)
     path = model_path(spec)
