@@ -8,10 +8,15 @@
 // memory, from where O += P.V runs on the tensor cores (M=128, N=64, K=64)
 // into TMEM (128 columns per CTA: S and O).
 // Two passes over the keys, as in the mma.sync kernels: the exact row maximum
-// must be known before any weight is exponentiated.
+// must be known before any weight is exponentiated.  P = 2^(S * 0.125 log2 e
+// - max * 0.125 log2 e), one fused multiply-add per two keys, with the
+// cutoff in the same base-2 units (softmax_tc.cuh, shared with the short
+// kernel).
 //
-//   warp 0      producer: TMA loads of Q (once) and of each key block's K
-//               (pass 1) or K and V (pass 2) into a 2-stage ring.
+//   warp 0      producer: TMA loads of Q (once), of each key block's K
+//               (both passes) into a 2-stage ring freed as soon as S has
+//               read it, and of its V (pass 2) into a second 2-stage ring
+//               freed by P.V, so the next K never waits behind a P.V.
 //   warp 1      TMEM allocation; one lane issues the MMAs: S(j+1) is issued
 //               before P(j).V (the softmax releases S as soon as it holds
 //               it in registers), so the softmax of block j overlaps it.
@@ -31,6 +36,7 @@
 #include <mutex>
 
 #include "kernels.h"
+#include "softmax_tc.cuh"
 #include "tcgen05.cuh"
 
 namespace le {
@@ -53,11 +59,13 @@ constexpr uint32_t IDESC_O = idesc_f16(BQ, HD) | (1u << 16);  // B (V) MN-major
 
 struct Lay {
   static constexpr int OFF_Q = 0;
-  static constexpr int OFF_KV = OFF_Q + Q_BYTES;         // [2 stages][K, V]
-  static constexpr int OFF_P = OFF_KV + 2 * 2 * KV_BYTES;
+  static constexpr int OFF_K = OFF_Q + Q_BYTES;       // [2 stages]
+  static constexpr int OFF_V = OFF_K + 2 * KV_BYTES;  // [2 stages]
+  static constexpr int OFF_P = OFF_V + 2 * KV_BYTES;
   static constexpr int OFF_BAR = OFF_P + P_BYTES;
-  // q_full, kv_full[2], kv_empty[2], s_full, s_empty, p_full, p_empty, o_full
-  static constexpr int NBAR = 10;
+  // q_full, k_full[2], k_empty[2], v_full[2], v_empty[2], s_full, s_empty,
+  // p_full, p_empty, o_full
+  static constexpr int NBAR = 14;
   static constexpr int OFF_MISC = OFF_BAR + NBAR * 8;
   static constexpr int BYTES = OFF_MISC + 16;
   static constexpr int ALLOC = BYTES + 1024;
@@ -89,10 +97,12 @@ __global__ void __launch_bounds__(NTHREADS, 3)
   const uint32_t sbase = smem_u32(smem);
   const uint32_t bar0 = sbase + Lay::OFF_BAR;
   const uint32_t q_full = bar0;
-  auto kv_full = [&](int s) { return bar0 + 8 * (1 + s); };
-  auto kv_empty = [&](int s) { return bar0 + 8 * (3 + s); };
-  const uint32_t s_full = bar0 + 8 * 5, s_empty = bar0 + 8 * 6;
-  const uint32_t p_full = bar0 + 8 * 7, p_empty = bar0 + 8 * 8, o_full = bar0 + 8 * 9;
+  auto k_full = [&](int s) { return bar0 + 8 * (1 + s); };
+  auto k_empty = [&](int s) { return bar0 + 8 * (3 + s); };
+  auto v_full = [&](int s) { return bar0 + 8 * (5 + s); };
+  auto v_empty = [&](int s) { return bar0 + 8 * (7 + s); };
+  const uint32_t s_full = bar0 + 8 * 9, s_empty = bar0 + 8 * 10;
+  const uint32_t p_full = bar0 + 8 * 11, p_empty = bar0 + 8 * 12, o_full = bar0 + 8 * 13;
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + Lay::OFF_MISC);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + Lay::OFF_MISC + 4);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -101,8 +111,10 @@ __global__ void __launch_bounds__(NTHREADS, 3)
     *abort_flag = 0;
     mbar_init(q_full, 1);
     for (int i = 0; i < 2; i++) {
-      mbar_init(kv_full(i), 1);
-      mbar_init(kv_empty(i), 1);
+      mbar_init(k_full(i), 1);
+      mbar_init(k_empty(i), 1);
+      mbar_init(v_full(i), 1);
+      mbar_init(v_empty(i), 1);
     }
     mbar_init(s_full, 1);
     mbar_init(s_empty, NSOFT);
@@ -130,19 +142,27 @@ __global__ void __launch_bounds__(NTHREADS, 3)
       // Q as two 64-row boxes: stacked, they form the 128-row swizzled tile.
       tma_load_2d(sbase + Lay::OFF_Q, &tmap, colq, t0 + qb * BQ, q_full);
       tma_load_2d(sbase + Lay::OFF_Q + KV_BYTES, &tmap, colq, t0 + qb * BQ + BKEY, q_full);
-      uint32_t it = 0;
+      uint32_t ik = 0, iv = 0;  // K and V ring counters
       bool ok = true;
       for (int pass = 0; pass < 2 && ok; pass++)
-        for (int j = 0; j < nkb; j++, it++) {
-          const int s = it & 1;
-          if (!mbar_wait(kv_empty(s), ((it >> 1) & 1) ^ 1, abort_flag, status, 31)) {
+        for (int j = 0; j < nkb; j++, ik++) {
+          const int s = ik & 1;
+          if (!mbar_wait(k_empty(s), ((ik >> 1) & 1) ^ 1, abort_flag, status, 31)) {
             ok = false;
             break;
           }
-          const uint32_t kdst = sbase + Lay::OFF_KV + s * 2 * KV_BYTES;
-          mbar_expect_tx(kv_full(s), pass == 0 ? KV_BYTES : 2 * KV_BYTES);
-          tma_load_2d(kdst, &tmap, colk, t0 + j * BKEY, kv_full(s));
-          if (pass == 1) tma_load_2d(kdst + KV_BYTES, &tmap, colv, t0 + j * BKEY, kv_full(s));
+          mbar_expect_tx(k_full(s), KV_BYTES);
+          tma_load_2d(sbase + Lay::OFF_K + s * KV_BYTES, &tmap, colk, t0 + j * BKEY, k_full(s));
+          if (pass == 1) {
+            const int v = iv & 1;
+            if (!mbar_wait(v_empty(v), ((iv >> 1) & 1) ^ 1, abort_flag, status, 30)) {
+              ok = false;
+              break;
+            }
+            mbar_expect_tx(v_full(v), KV_BYTES);
+            tma_load_2d(sbase + Lay::OFF_V + v * KV_BYTES, &tmap, colv, t0 + j * BKEY, v_full(v));
+            iv++;
+          }
         }
     }
   } else if (warp == 1) {
@@ -151,50 +171,52 @@ __global__ void __launch_bounds__(NTHREADS, 3)
       bool ok = mbar_wait(q_full, 0, abort_flag, status, 32);
       tc_fence_after();
       const uint32_t qaddr = sbase + Lay::OFF_Q;
-      uint32_t it = 0, sn = 0;  // key-block counter (stages), S use counter
-      // S(j) = Q . K(j)^T into the S columns, once the softmax has read the last S.
-      auto issue_s = [&](uint32_t stage_it) -> bool {
-        const int s = stage_it & 1;
-        if (!mbar_wait(kv_full(s), (stage_it >> 1) & 1, abort_flag, status, 33) ||
+      uint32_t ik = 0, sn = 0;  // K ring counter, S use counter
+      // S(j) = Q . K(j)^T into the S columns, once the softmax has read the
+      // last S; the K stage is free once S is computed.
+      auto issue_s = [&]() -> bool {
+        const int s = ik & 1;
+        if (!mbar_wait(k_full(s), (ik >> 1) & 1, abort_flag, status, 33) ||
             !mbar_wait(s_empty, (sn & 1) ^ 1, abort_flag, status, 34))
           return false;
         tc_fence_after();
-        const uint32_t kaddr = sbase + Lay::OFF_KV + s * 2 * KV_BYTES;
+        const uint32_t kaddr = sbase + Lay::OFF_K + s * KV_BYTES;
 #pragma unroll
         for (int kk = 0; kk < HD / 16; kk++)
           mma_f16(tmem, sw128_desc(qaddr + kk * 32), sw128_desc(kaddr + kk * 32), IDESC_S, kk != 0);
         mma_commit(s_full);
+        mma_commit(k_empty(s));
         sn++;
+        ik++;
         return true;
       };
-      // Pass 1: scores only; the K stage is free once its S is computed.
-      for (int j = 0; j < nkb && ok; j++, it++) {
-        ok = issue_s(it);
-        if (ok) mma_commit(kv_empty(it & 1));
-      }
-      // Pass 2: S(j), then P(j-1).V(j-1), which frees block j-1's stage.
-      uint32_t pn = 0;
-      auto issue_pv = [&](uint32_t stage_it, bool first) -> bool {
-        const int s = stage_it & 1;
-        if (!mbar_wait(p_full, pn & 1, abort_flag, status, 35)) return false;
+      // Pass 1: scores only.
+      for (int j = 0; j < nkb && ok; j++) ok = issue_s();
+      // Pass 2: S(j), then P(j-1).V(j-1), which frees V's stage and P.
+      uint32_t pn = 0, iv = 0;
+      auto issue_pv = [&](bool first) -> bool {
+        const int v = iv & 1;
+        if (!mbar_wait(p_full, pn & 1, abort_flag, status, 35) ||
+            !mbar_wait(v_full(v), (iv >> 1) & 1, abort_flag, status, 37))
+          return false;
         tc_fence_after();
-        const uint32_t vaddr = sbase + Lay::OFF_KV + s * 2 * KV_BYTES + KV_BYTES;
+        const uint32_t vaddr = sbase + Lay::OFF_V + v * KV_BYTES;
         const uint32_t paddr = sbase + Lay::OFF_P;
 #pragma unroll
         for (int kk = 0; kk < BKEY / 16; kk++)
           mma_f16(tmem + BKEY, sw128_desc(paddr + kk * 32), sw128_desc(vaddr + kk * 2048), IDESC_O,
                   !(first && kk == 0));
-        mma_commit(kv_empty(s));
+        mma_commit(v_empty(v));
         mma_commit(p_empty);
         pn++;
+        iv++;
         return true;
       };
-      const uint32_t it2 = it;
-      for (int j = 0; j < nkb && ok; j++, it++) {
-        ok = issue_s(it);
-        if (ok && j > 0) ok = issue_pv(it - 1, j == 1);
+      for (int j = 0; j < nkb && ok; j++) {
+        ok = issue_s();
+        if (ok && j > 0) ok = issue_pv(j == 1);
       }
-      if (ok) ok = issue_pv(it2 + nkb - 1, nkb == 1);
+      if (ok) ok = issue_pv(nkb == 1);
       if (ok) mma_commit(o_full);
     }
   } else {
@@ -205,7 +227,7 @@ __global__ void __launch_bounds__(NTHREADS, 3)
     uint8_t* prow = smem + Lay::OFF_P + row * 128;
     bool ok = true;
     uint32_t sn = 0, pn = 0;
-    float mx = -INFINITY;
+    float m0 = -INFINITY, m1 = -INFINITY;
     for (int j = 0; j < nkb; j++, sn++) {
       ok = ok && __all_sync(0xffffffffu, mbar_wait(s_full, sn & 1, abort_flag, status, 36));
       uint32_t r[64];
@@ -219,20 +241,16 @@ __global__ void __launch_bounds__(NTHREADS, 3)
       __syncwarp();
       if (lane == 0) mbar_arrive(s_empty);
       if (ok) {
-        // Maximum of the raw scores; scaling by 0.125 (exact) afterwards.
-        const int kmax = L - j * BKEY;  // keys < kmax are valid
-        if (kmax >= BKEY) {
+        // Maximum of the raw scores of keys < L.
+        const int kmax = L - j * BKEY;
 #pragma unroll
-          for (int i = 0; i < 64; i++) mx = fmaxf(mx, __uint_as_float(r[i]));
-        } else {
-#pragma unroll
-          for (int i = 0; i < 64; i++)
-            if (i < kmax) mx = fmaxf(mx, __uint_as_float(r[i]));
-        }
+        for (int c = 0; c < BKEY / 16; c++)
+          if (16 * c < kmax) chunk_max<16>(m0, m1, r + 16 * c, kmax - 16 * c);
       }
     }
-    mx *= 0.125f;
-    float l = 0.f;
+    const float mx = fmaxf(m0, m1);
+    const unsigned long long scale = f2_pack(SCALE2, SCALE2), off = f2_pack(-mx * SCALE2, -mx * SCALE2);
+    unsigned long long s0 = f2_pack(0.f, 0.f), s1 = s0;
     for (int j = 0; j < nkb; j++, sn++, pn++) {
       ok = ok && __all_sync(0xffffffffu, mbar_wait(s_full, sn & 1, abort_flag, status, 38));
       uint32_t r[64];
@@ -248,27 +266,15 @@ __global__ void __launch_bounds__(NTHREADS, 3)
       ok = ok && __all_sync(0xffffffffu, mbar_wait(p_empty, (pn & 1) ^ 1, abort_flag, status, 39));
       if (ok) {
         // P row `row` = 8 chunks of 8 fp16 keys in the 128-byte-swizzled
-        // K-major layout; masked keys get weight 0.
+        // K-major layout, 16 keys per step; keys past the sequence get
+        // weight 0.
         const int kmax = L - j * BKEY;
-        if (kmax < BKEY) {
 #pragma unroll
-          for (int i = 0; i < 64; i++)
-            if (i >= kmax) r[i] = __float_as_uint(-INFINITY);
-        }
-#pragma unroll
-        for (int c = 0; c < 8; c++) {
-          uint32_t w[4];
-#pragma unroll
-          for (int e = 0; e < 4; e++) {
-            const int i0 = 8 * c + 2 * e;
-            const float d0 = __fsub_rn(__uint_as_float(r[i0]) * 0.125f, mx);
-            const float d1 = __fsub_rn(__uint_as_float(r[i0 + 1]) * 0.125f, mx);
-            // P is rounded to fp16: the fast exponential's error is far below it.
-            const float p0 = d0 < -10.f ? 0.f : __expf(d0), p1 = d1 < -10.f ? 0.f : __expf(d1);
-            l += p0 + p1;
-            w[e] = pack_half2(p0, p1);
-          }
-          *reinterpret_cast<uint4*>(prow + ((c ^ (row & 7)) << 4)) = make_uint4(w[0], w[1], w[2], w[3]);
+        for (int c = 0; c < BKEY / 16; c++) {
+          uint32_t w[8];
+          chunk_p<16>(r + 16 * c, kmax - 16 * c, scale, off, s0, s1, w);
+          *reinterpret_cast<uint4*>(prow + (((2 * c) ^ (row & 7)) << 4)) = make_uint4(w[0], w[1], w[2], w[3]);
+          *reinterpret_cast<uint4*>(prow + (((2 * c + 1) ^ (row & 7)) << 4)) = make_uint4(w[4], w[5], w[6], w[7]);
         }
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
       }
@@ -278,7 +284,9 @@ __global__ void __launch_bounds__(NTHREADS, 3)
     ok = ok && __all_sync(0xffffffffu, mbar_wait(o_full, 0, abort_flag, status, 41));
     if (ok) {
       tc_fence_after();
-      const float inv = 1.0f / l;
+      float l0, l1;
+      f2_unpack(f2_add(s0, s1), l0, l1);
+      const float inv = 1.0f / (l0 + l1);
       uint32_t r[64];
       tmem_ld32_nowait(tmem + lane_off + BKEY, r);
       tmem_ld32_nowait(tmem + lane_off + BKEY + 32, r + 32);
