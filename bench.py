@@ -28,6 +28,7 @@ synchronize; times are the max over ranks.  Rank 0 prints one JSON line.
             infrastructure) on this host's cores, rank 0, N=1.
 
 Extra keys: weak scaling (N>1: each rank its own 256-sequence batch),
+the optional NCCL all-gather of the embeddings (N>1, outside the timed step),
 per-rank shard sizes and kernel times, configs[3] and configs[4] at their
 stated sizes (sharded the same way), the configs[1] op sweep (N=1), model
 load phases (f2) and host tokenizer throughput (f1).
@@ -405,6 +406,36 @@ def headline(ctx, args, pk, res):
                            "ms_per_step": sum(step_ms) / args.steps, "kernel_ms_per_step": kernel_ms,
                            "gpu_launches_per_step": launches / args.steps, "clocks": clk})
 
+    gather = None
+    if ctx.world > 1:
+        # The optional collective of the multi-GPU row: every rank's
+        # embeddings to every rank (NCCL all-gather over NVLink), shards
+        # padded to the largest one.  Not part of the path or of `value`.
+        counts = [int(ldist.local_shard(ids, offs, r, ctx.world)[1].size - 1) for r in range(ctx.world)]
+        mx = max(counts)
+        send = torch.zeros(mx, H, device="cuda")
+        send[:b.nseq].copy_(b.out[:b.nseq])
+        recv = torch.empty(ctx.world * mx, H, device="cuda")
+        for _ in range(3):
+            ctx.dist.all_gather_into_tensor(recv, send)
+        torch.cuda.synchronize()
+        ctx.barrier()
+        g0, g1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        reps = 20
+        g0.record(ctx.stream)
+        for _ in range(reps):
+            ctx.dist.all_gather_into_tensor(recv, send)
+        g1.record(ctx.stream)
+        torch.cuda.synchronize()
+        g_ms = ctx.max(g0.elapsed_time(g1) / reps)
+        got = recv.view(ctx.world, mx, H)[ctx.rank, :b.nseq]
+        assert torch.equal(got, b.out[:b.nseq])
+        nbytes = ctx.world * mx * H * 4
+        gather = {"ms": g_ms, "bytes_gathered": nbytes, "algbw_gbs": nbytes / (g_ms * 1e6),
+                  "busbw_gbs": nbytes * (ctx.world - 1) / ctx.world / (g_ms * 1e6),
+                  "note": "NCCL all_gather_into_tensor of every rank's [max shard x 768] f32 embeddings, CUDA events "
+                          "on the bench stream, mean of 20 after 3 warm-up, max over ranks; outside the timed step"}
+
     weak = None
     if ctx.world > 1:
         # Weak scaling: every rank its own 256-sequence batch (seed 1 + rank).
@@ -457,6 +488,8 @@ def headline(ctx, args, pk, res):
         })
         if weak:
             res["weak_scaling"] = weak
+        if gather:
+            res["allgather_embeddings"] = gather
         res["clocks"]["reasons"] = sorted({r for p in per_rank for r in (p["clocks"] or {}).get("reasons", [])})
     return e
 
