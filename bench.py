@@ -567,7 +567,8 @@ def other_configs(ctx, args, pk, res):
 
 def op_sweep(ctx, pk, res):
     """le_qgemm_device (fp32 x in, fp32 y out) over M x K x N x
-    type, median of 5 calls with L2 flushed between them."""
+    type, median of 5 calls with L2 flushed between them (the GPU kept ahead
+    of the host, so the events time the two kernels of a call)."""
     from llm_embed_b200.embed import QWeight
     torch = ctx.torch
     rows = []
@@ -589,6 +590,7 @@ def op_sweep(ctx, pk, res):
                     ts = []
                     for _ in range(5):
                         ctx.flush.zero_()
+                        torch.cuda._sleep(1_000_000)  # the GPU ahead of the host's enqueue
                         a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
                         a.record(ctx.stream)
                         qw.matmul_device(x.data_ptr(), M, y.data_ptr(), ctx.stream.cuda_stream)
