@@ -27,6 +27,10 @@ __device__ __forceinline__ double warp_sum_d(double v) {
 // invStd = float32(1 / sqrt(float64(var + eps))), y = (x-mean)*invStd*w + b.
 // H is a multiple of 128 and at most 128 * LN_MAXV.
 constexpr int LN_MAXV = 8;  // float4 per lane -> H <= 1024
+// Staged bytes of one embedding row per warp: an F32 row of 1,024 values
+// plus the 16 bytes before its boundary, in 16-byte loads (32 lanes x 9).
+constexpr int EMB_STAGE = 32 * 16 * 9;
+static_assert(EMB_STAGE >= 4 * 128 * LN_MAXV + 16, "the widest row fits");
 
 template <bool GATHER>
 __global__ void __launch_bounds__(256) ln_rows_kernel(const float* in, const float* __restrict__ add,
@@ -45,12 +49,29 @@ __global__ void __launch_bounds__(256) ln_rows_kernel(const float* in, const flo
   float4 x[LN_MAXV];
   if constexpr (GATHER) {
     // bert.go:227-247: token_embd row + token_types row 0, then LayerNorm.
+    // The row's bytes come first into the warp's shared-memory slot with
+    // 16-byte loads from the 16-byte boundary at or below the row (the
+    // embedding buffer carries 16 spare bytes), all in flight at once; the
+    // values are then decoded from there.
+    __shared__ __align__(16) uint8_t stage[8][EMB_STAGE];
     int id = ids[warp];
     if (id < 0 || id >= vocab) {  // device-resident ids are not checked on the host
       if (lane == 0) report(status, DE_BOUNDS, 1, id);
       id = 0;
     }
-    const uint8_t* row = emb + (long)id * emb_row_bytes;
+    const uintptr_t ra = reinterpret_cast<uintptr_t>(emb + (long)id * emb_row_bytes);
+    const uint4* src = reinterpret_cast<const uint4*>(ra & ~(uintptr_t)15);
+    const int n16 = (int)(((ra & 15) + emb_row_bytes + 15) >> 4);
+    uint8_t* st = stage[(threadIdx.x >> 5) & 7];
+    uint4 q[EMB_STAGE / 16 / 32];
+#pragma unroll
+    for (int k = 0; k < EMB_STAGE / 16 / 32; k++)
+      if (lane + 32 * k < n16) q[k] = __ldg(src + lane + 32 * k);
+#pragma unroll
+    for (int k = 0; k < EMB_STAGE / 16 / 32; k++)
+      if (lane + 32 * k < n16) *reinterpret_cast<uint4*>(st + 16 * (lane + 32 * k)) = q[k];
+    __syncwarp();
+    const uint8_t* row = st + (ra & 15);
 #pragma unroll
     for (int i = 0; i < LN_MAXV; i++) {
       if (i < nv) {
@@ -170,7 +191,7 @@ __global__ void positions_kernel(const int32_t* __restrict__ offsets, int nseq, 
 cudaError_t launch_embed_ln(const int32_t* ids, int emb_type, const uint8_t* emb, long emb_row_bytes, int vocab,
                             const float* type0, const float* w, const float* b, float eps, int T, int H, float* out32,
                             __half* out16, DevStatus* status, cudaStream_t s) {
-  if (H % 128 || H > 128 * LN_MAXV) return cudaErrorInvalidValue;
+  if (H % 128 || H > 128 * LN_MAXV || emb_row_bytes + 16 > EMB_STAGE) return cudaErrorInvalidValue;
   if (T == 0) return cudaSuccess;
   cudaLaunchAttribute attr[1];
   const cudaLaunchConfig_t cfg = pdl_config(dim3((T + 7) / 8), dim3(256), 0, s, attr);
