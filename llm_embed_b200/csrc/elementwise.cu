@@ -127,12 +127,21 @@ __global__ void pool_kernel(const float* __restrict__ h, const int32_t* __restri
   __shared__ double red[32];
   float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
   if (c < H) {
-    for (int t = t0; t < t1; t++) {
-      const float4 v = *reinterpret_cast<const float4*>(h + (long)t * H + c);
-      acc.x += v.x;
-      acc.y += v.y;
-      acc.z += v.z;
-      acc.w += v.w;
+    // Eight rows' loads in flight, added in token order.
+    constexpr int U = 8;
+    for (int t = t0; t < t1; t += U) {
+      float4 v[U];
+#pragma unroll
+      for (int u = 0; u < U; u++)
+        if (t + u < t1) v[u] = __ldcs(reinterpret_cast<const float4*>(h + (long)(t + u) * H + c));
+#pragma unroll
+      for (int u = 0; u < U; u++)
+        if (t + u < t1) {
+          acc.x += v[u].x;
+          acc.y += v[u].y;
+          acc.z += v[u].z;
+          acc.w += v[u].w;
+        }
     }
     if (t1 > t0) {
       const float inv = __fdiv_rn(1.0f, (float)(t1 - t0));
