@@ -4,7 +4,7 @@
 // At batch 1 the forward is a chain of small dependent steps over 120 MB of
 // weights (Q8_0).  Weights never depend on activations, so each CTA streams
 // the weight pages of its share of every step into a shared-memory ring
-// ahead of use (TMA bulk copies, mbarrier-tracked: thread 0 issues page k + R
+// ahead of use (TMA bulk copies, mbarrier-tracked: one thread issues page k + R
 // as soon as the warps are done with page k), and the chain itself only
 // waits for the activations other CTAs produce.
 //
@@ -52,6 +52,10 @@ constexpr int HD = H / HEADS;
 constexpr int NCW = r16::WARPS;            // warps (the K split of gemm_r16.cuh)
 constexpr int NTHREADS = NCW * 32;
 constexpr int NCT = NTHREADS;
+// The thread that issues the weight pages' bulk copies: the CTA's last,
+// which has no output item of a step's reduction at 8 tokens (thread 0 also
+// polls the hand-off counters), so the issue is off the step's critical path.
+constexpr int ISSUER = NCT - 1;
 constexpr int LDX = H + 8;                 // padded fp16 row stride of x
 // A page is one work item: a 16-row tile's K slice (gemm_r16.cuh: K = 768 is
 // one slice of 12 chunks, K = 3072 three of 16), contiguous in the row16
@@ -318,14 +322,14 @@ __device__ void attention_head(const SmallParams& p, uint8_t* U, int head) {
 }
 
 // The CTA's page sequence (every step's work items in consumption order),
-// walked by thread 0 as it issues the pages' bulk copies: page k goes to ring
+// walked by the ISSUER thread as it issues the pages' bulk copies: page k goes to ring
 // slot k % R once page k - R has been consumed.
 struct PageIter {
   int l = 0, m = 0, it = 0, t1 = -1;
   uint32_t issued = 0;  // pages issued so far
 };
 
-// Issue the next page of the sequence into its slot (thread 0); false when
+// Issue the next page of the sequence into its slot (ISSUER); false when
 // the sequence is exhausted.
 template <class SH>
 __device__ bool issue_next(const SmallParams& p, const SH& S, PageIter& pi) {
@@ -353,7 +357,7 @@ __device__ bool issue_next(const SmallParams& p, const SH& S, PageIter& pi) {
   return false;
 }
 
-// Thread 0 before the CTA exits: every issued copy has landed (a CTA must not
+// ISSUER before the CTA exits: every issued copy has landed (a CTA must not
 // exit with bulk copies into its shared memory in flight).
 template <class SH>
 __device__ void drain(const SH& S, const PageIter& pi) {
@@ -443,7 +447,7 @@ __device__ bool gemm_tiles(const SmallParams& p, const SH& S, PageIter& pi, cons
   bar_compute();
   // The items' pages are consumed: their slots take the next pages (the
   // proxy fence orders the warps' reads before the copies' writes).
-  if (threadIdx.x == 0) {
+  if (threadIdx.x == ISSUER) {
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
     for (int q = 0; q < n; q++) issue_next(p, S, pi);
   }
@@ -498,8 +502,8 @@ __global__ void __launch_bounds__(NTHREADS, 1) forward_small_kernel(const __grid
   S.flag = reinterpret_cast<volatile int*>(smem + L::OFF_MISC + 4);
   const int T = p.T;
 
-  PageIter pi;
-  if (threadIdx.x == 0) {
+  PageIter pi;  // (meaningful in the ISSUER thread)
+  if (threadIdx.x == ISSUER) {
     for (int i = 0; i < L::R; i++) mbar_init(S.bar0 + 8 * i, 1);
     *S.abort = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -647,7 +651,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) forward_small_kernel(const __grid
     for (int i = threadIdx.x; i < T * H; i += NCT) p.h_out[i] = S.h[i];
   }
 out:
-  if (threadIdx.x == 0) drain(S, pi);
+  if (threadIdx.x == ISSUER) drain(S, pi);
 }
 
 }  // namespace fs
