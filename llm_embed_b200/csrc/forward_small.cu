@@ -84,16 +84,19 @@ struct Lay {
   static constexpr int X_BYTES = TS * LDX * 2;
   static constexpr int U_BYTES = X_BYTES > NCW * ATT_WARP_BYTES ? X_BYTES : NCW * ATT_WARP_BYTES;
   static constexpr int RED_BYTES = MAX_TILES * NCW * NT * 32 * 16;
-  static constexpr int FIXED = H_BYTES + U_BYTES + RED_BYTES + MAX_SLOTS * 8 + 64;
+  static constexpr int STEP_BYTES = SMALL_MAX_LAYERS * 4 * 8;  // the page walk's per-step cache
+  static constexpr int FIXED = H_BYTES + U_BYTES + RED_BYTES + STEP_BYTES + MAX_SLOTS * 8 + 64;
   static constexpr int R = (SMEM_MAX - FIXED) / SLOT < MAX_SLOTS ? (SMEM_MAX - FIXED) / SLOT : MAX_SLOTS;
   static constexpr int OFF_RING = 0;
   static constexpr int OFF_H = R * SLOT;
   static constexpr int OFF_U = OFF_H + H_BYTES;
   static constexpr int OFF_RED = OFF_U + U_BYTES;
-  static constexpr int OFF_BAR = OFF_RED + RED_BYTES;  // full[R]
+  static constexpr int OFF_STEP = OFF_RED + RED_BYTES;  // int2 info[l][m]
+  static constexpr int OFF_BAR = OFF_STEP + STEP_BYTES;  // full[R]
   static constexpr int OFF_MISC = OFF_BAR + R * 8;
   static constexpr int BYTES = OFF_MISC + 64;
   static_assert(R >= MAX_TILES + 1, "the ring must hold a step's pages and the next one");
+  static_assert(OFF_STEP % 16 == 0, "step cache alignment");
   static_assert(BYTES <= SMEM_MAX, "shared memory budget");
 };
 
@@ -133,6 +136,7 @@ struct SharedT {
   __half* x;
   uint8_t* U;
   float4* red;
+  const int2* step_info;  // per (layer, step): {K | qf << 16, first item | end item << 16} of this CTA
   uint32_t bar0;
   volatile int* abort;
   volatile int* flag;
@@ -326,7 +330,8 @@ __device__ void attention_head(const SmallParams& p, uint8_t* U, int head) {
 // slot k % R once page k - R has been consumed.
 struct PageIter {
   int l = 0, m = 0, it = 0, t1 = -1;
-  uint32_t issued = 0;  // pages issued so far
+  uint32_t issued = 0;        // pages issued so far
+  const uint8_t* w = nullptr;  // the current step's row16 weight
 };
 
 // Issue the next page of the sequence into its slot (ISSUER); false when
@@ -334,14 +339,20 @@ struct PageIter {
 template <class SH>
 __device__ bool issue_next(const SmallParams& p, const SH& S, PageIter& pi) {
   while (pi.l < p.n_layers) {
-    const SmallGemm& g = p.layers[pi.l].g[pi.m];
-    if (pi.t1 < 0) tile_range(pi.m, items_of(g), &pi.it, &pi.t1);
+    const int sx = pi.l * 4 + pi.m;
+    const int2 inf = S.step_info[sx];
+    if (pi.t1 < 0) {
+      pi.it = inf.y & 0xFFFF;
+      pi.t1 = inf.y >> 16;
+      pi.w = p.layers[pi.l].g[pi.m].w;
+    }
     if (pi.it < pi.t1) {
-      const int ns = r16::n_slices(g.K), tile = pi.it / ns, slice = pi.it % ns;
+      const int K = inf.x & 0xFFFF, cb = r16::chunk_bytes(inf.x >> 16), nch = K / TILE_K;
+      const int ns = r16::n_slices(K), tile = pi.it / ns, slice = pi.it % ns;
+      const int c0 = slice * (r16::KSLICE / TILE_K);
       const uint32_t slot = pi.issued % SH::R;
-      const uint32_t bytes = page_chunks(g, slice) * r16::chunk_bytes(g.qf);
-      const uint8_t* src = g.w + (long)tile * (g.K / TILE_K) * r16::chunk_bytes(g.qf) +
-                           (long)slice * (r16::KSLICE / TILE_K) * r16::chunk_bytes(g.qf);
+      const uint32_t bytes = (uint32_t)((nch - c0 < r16::KSLICE / TILE_K ? nch - c0 : r16::KSLICE / TILE_K) * cb);
+      const uint8_t* src = pi.w + ((long)tile * nch + c0) * cb;
       mbar_expect_tx(S.bar0 + 8 * slot, bytes);
       bulk_load(tcx::smem_u32(S.ring + slot * SLOT), src, bytes, S.bar0 + 8 * slot);
       pi.it++;
@@ -497,11 +508,23 @@ __global__ void __launch_bounds__(NTHREADS, 1) forward_small_kernel(const __grid
   S.U = smem + L::OFF_U;
   S.x = reinterpret_cast<__half*>(S.U);
   S.red = reinterpret_cast<float4*>(smem + L::OFF_RED);
+  S.step_info = reinterpret_cast<const int2*>(smem + L::OFF_STEP);
   S.bar0 = tcx::smem_u32(smem + L::OFF_BAR);
   S.abort = reinterpret_cast<volatile int*>(smem + L::OFF_MISC);
   S.flag = reinterpret_cast<volatile int*>(smem + L::OFF_MISC + 4);
   const int T = p.T;
 
+  // The page walk's per-step cache: K, format and this CTA's items of step
+  // (l, m), one thread per step (the walk then needs no division of the
+  // grid and no parameter loads per page).
+  if (threadIdx.x < p.n_layers * 4) {
+    const int l = threadIdx.x >> 2, m = threadIdx.x & 3;
+    const SmallGemm& g = p.layers[l].g[m];
+    int t0, t1;
+    tile_range(m, items_of(g), &t0, &t1);
+    reinterpret_cast<int2*>(smem + L::OFF_STEP)[threadIdx.x] = make_int2(g.K | (g.qf << 16), t0 | (t1 << 16));
+  }
+  __syncthreads();
   PageIter pi;  // (meaningful in the ISSUER thread)
   if (threadIdx.x == ISSUER) {
     for (int i = 0; i < L::R; i++) mbar_init(S.bar0 + 8 * i, 1);
