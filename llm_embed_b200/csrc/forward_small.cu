@@ -75,7 +75,13 @@ constexpr int CNT_ATT = HEADS;
 constexpr int CNT_Y1 = HEADS + 1;
 constexpr int CNT_FF = HEADS + 2;
 constexpr int CNT_Y2 = HEADS + 3;
-constexpr int N_CNT = HEADS + 4;
+constexpr int CNT_QKV_ALL = HEADS + 4;  // QKV tiles done, every head (calls of one sequence)
+constexpr int N_CNT = HEADS + 5;
+// Calls of one sequence of at most 8 tokens: every output-projection CTA
+// computes all the heads' attention itself (AW warps, two rounds) into its
+// shared memory after the per-warp staging, instead of 12 attention CTAs
+// and two more hand-offs.
+constexpr int AW = 6;
 
 template <int NT>
 struct Lay {
@@ -97,6 +103,8 @@ struct Lay {
   static constexpr int BYTES = OFF_MISC + 64;
   static_assert(R >= MAX_TILES + 1, "the ring must hold a step's pages and the next one");
   static_assert(OFF_STEP % 16 == 0, "step cache alignment");
+  static_assert(NT != 1 || AW * ATT_WARP_BYTES + 8 * LDX * 2 <= U_BYTES, "one-sequence attention output");
+  static_assert((AW * ATT_WARP_BYTES) % 16 == 0, "attention output alignment");
   static_assert(BYTES <= SMEM_MAX, "shared memory budget");
 };
 
@@ -325,6 +333,36 @@ __device__ void attention_head(const SmallParams& p, uint8_t* U, int head) {
   }
 }
 
+// Attention of every head for a call of one sequence (t0 = 0, L = T), on
+// an output-projection CTA: heads over warps 0..AW-1, each staged and
+// computed exactly as attention_head stages and computes a sequence, the
+// output into `att` (row stride LDX, shared memory).
+__device__ void attention_all_heads(const SmallParams& p, uint8_t* U, __half* att) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (warp >= AW) return;
+  __half(*sQ)[attn::LDS] = reinterpret_cast<__half(*)[attn::LDS]>(U + warp * ATT_WARP_BYTES);
+  __half(*sK)[attn::LDS] = sQ + 16;
+  __half(*sV)[attn::LDS] = sK + 16;
+  const int L = p.T;
+  for (int head = warp; head < HEADS; head += AW) {
+    uint4 v[12];
+#pragma unroll
+    for (int j = 0; j < 12; j++) {
+      const int i = lane + 32 * j, which = i >> 7, r = (i >> 3) & 15, c = (i & 7) * 8;
+      v[j] = r < L ? __ldcg(reinterpret_cast<const uint4*>(p.qkv + (long)r * 3 * H + which * H + head * HD + c))
+                   : make_uint4(0, 0, 0, 0);
+    }
+#pragma unroll
+    for (int j = 0; j < 12; j++) {
+      const int i = lane + 32 * j, which = i >> 7, r = (i >> 3) & 15, c = (i & 7) * 8;
+      *reinterpret_cast<uint4*>(&sQ[which * 16 + r][c]) = v[j];
+    }
+    __syncwarp();
+    attn::attn_rows16(sQ, 0, sK, sV, L, att + head * HD, LDX, 0);
+    __syncwarp();
+  }
+}
+
 // The CTA's page sequence (every step's work items in consumption order),
 // walked by the ISSUER thread as it issues the pages' bulk copies: page k goes to ring
 // slot k % R once page k - R has been consumed.
@@ -507,6 +545,10 @@ __global__ void __launch_bounds__(NTHREADS, 1) forward_small_kernel(const __grid
   S.h = reinterpret_cast<float*>(smem + L::OFF_H);
   S.U = smem + L::OFF_U;
   S.x = reinterpret_cast<__half*>(S.U);
+  // One sequence of at most 8 tokens: the attention output goes after the
+  // AW warps' staging areas (past x, which the output phase does not read).
+  const bool one_seq = NT == 1 && p.nseq == 1;
+  __half* att_s = reinterpret_cast<__half*>(S.U + AW * ATT_WARP_BYTES);
   S.red = reinterpret_cast<float4*>(smem + L::OFF_RED);
   S.step_info = reinterpret_cast<const int2*>(smem + L::OFF_STEP);
   S.bar0 = tcx::smem_u32(smem + L::OFF_BAR);
@@ -595,11 +637,11 @@ __global__ void __launch_bounds__(NTHREADS, 1) forward_small_kernel(const __grid
           if (!gemm_tiles_any<NT, 3, false>(p, S, pi, g, t, 1, seq, S.x, nullptr, 0, ep)) goto out;
         }
         seq += 1;
-        signal(p, CNT_QKV + ((16 * t) % H) / HD);
+        signal(p, one_seq ? CNT_QKV_ALL : CNT_QKV + ((16 * t) % H) / HD);
       }
     }
     // ---- Attention of one head, once its 12 QKV tiles are in.
-    for (int hd = 0; hd < HEADS; hd++) {
+    for (int hd = 0; hd < HEADS && !one_seq; hd++) {
       if (att_cta(hd) != (int)blockIdx.x) continue;
       if (!wait_cnt(p, S, CNT_QKV + hd, (unsigned)(3 * HD / 16 * (l + 1)), 71)) goto out;
       attention_head(p, S.U, hd);
@@ -610,17 +652,30 @@ __global__ void __launch_bounds__(NTHREADS, 1) forward_small_kernel(const __grid
       const SmallGemm& g = Ly.g[1];
       int t0, t1;
       tile_range(1, items_of(g), &t0, &t1);
-      if (t1 > t0 && !wait_cnt(p, S, CNT_ATT, (unsigned)(HEADS * (l + 1)), 72)) goto out;
       EpiParams ep{};
       ep.M = T;
       ep.mode = EPI_F32;
       ep.N = H;
       ep.out32 = p.y1;
       ep.ldo = H;
-      for (int t = t0; t < t1; t++) {
-        if (!gemm_tiles_any<NT, 3, true>(p, S, pi, g, t, 1, seq, nullptr, p.att, H, ep)) goto out;
-        seq += 1;
-        signal(p, CNT_Y1);
+      if (one_seq) {
+        if (t1 > t0) {
+          if (!wait_cnt(p, S, CNT_QKV_ALL, (unsigned)(items_of(Ly.g[0]) * (l + 1)), 72)) goto out;
+          attention_all_heads(p, S.U, att_s);
+          bar_compute();
+        }
+        for (int t = t0; t < t1; t++) {
+          if (!gemm_tiles_any<NT, 3, false>(p, S, pi, g, t, 1, seq, att_s, nullptr, 0, ep)) goto out;
+          seq += 1;
+          signal(p, CNT_Y1);
+        }
+      } else {
+        if (t1 > t0 && !wait_cnt(p, S, CNT_ATT, (unsigned)(HEADS * (l + 1)), 72)) goto out;
+        for (int t = t0; t < t1; t++) {
+          if (!gemm_tiles_any<NT, 3, true>(p, S, pi, g, t, 1, seq, nullptr, p.att, H, ep)) goto out;
+          seq += 1;
+          signal(p, CNT_Y1);
+        }
       }
     }
     // ---- Up/gate: residual LayerNorm after attention, GEGLU tiles.
