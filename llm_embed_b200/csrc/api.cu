@@ -477,7 +477,7 @@ static int forward(le_model* m, const int32_t* d_ids, const int32_t* d_offsets, 
   unsigned* ln_ctl = w.ln_ctl.as<unsigned>();
   const int ln_rows = gemm_ln_part_rows(w.cap_tokens);
   if (T > 0 && T <= SMALL_MAX_TOKENS && (int)m->layers.size() <= SMALL_MAX_LAYERS) {
-    // A few tokens: the whole encoder in one cooperative kernel, then the pool.
+    // A few tokens: the whole encoder and the pool in one cooperative kernel.
     SmallParams sp{};
     sp.T = T;
     sp.nseq = nseq;
@@ -500,7 +500,8 @@ static int forward(le_model* m, const int32_t* d_ids, const int32_t* d_offsets, 
     sp.y1 = y32;
     sp.y2 = y32 + (size_t)SMALL_MAX_TOKENS * H;
     sp.ff = ff;
-    sp.h_out = h32;
+    sp.out = d_out;
+    sp.out_dim = out_dim;
     sp.sync = m->barrier.as<unsigned>();
     sp.status = m->status.as<DevStatus>();
     for (int l = 0; l < sp.n_layers; l++) {
@@ -517,7 +518,6 @@ static int forward(le_model* m, const int32_t* d_ids, const int32_t* d_offsets, 
     }
     if (small_forward_supported(sp, H, F, m->hp.heads, m->sms)) {
       PLAUNCH(8, launch_forward_small(sp, s));
-      PLAUNCH(7, launch_pool(h32, d_offsets, nseq, H, out_dim, d_out, s));
       return LE_OK;
     }
   }

@@ -9,15 +9,11 @@
 #include "gguf_decode.cuh"
 #include "kernels.h"
 #include "ln_warp.cuh"
+#include "pool_seq.cuh"
 
 namespace le {
 
 __device__ __forceinline__ float warp_sum(float v) {
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-  return v;
-}
-__device__ __forceinline__ double warp_sum_d(double v) {
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
   return v;
@@ -113,66 +109,15 @@ __global__ void __launch_bounds__(256) ln_rows_kernel(const float* in, const flo
     }
 }
 
-// pool.go:8-53 + embedder.go:59-68: masked mean (f32 sum, x (1/count)),
-// L2 normalise (float64 sum of squares, float32 multiply by float32(1/norm)),
-// then Matryoshka truncation to out_dim and renormalisation.  One CTA of
-// H/4 threads per sequence; empty sequences give a zero vector.
+// pool.go:8-53 + embedder.go:59-68 (pool_seq.cuh): one CTA of H/4 threads
+// per sequence.
 __global__ void pool_kernel(const float* __restrict__ h, const int32_t* __restrict__ offsets, int H, int out_dim,
                             float* __restrict__ out) {
   pdl_wait();
   pdl_trigger();
   const int s = blockIdx.x;
-  const int t0 = offsets[s], t1 = offsets[s + 1];
-  const int c = threadIdx.x * 4;
   __shared__ double red[32];
-  float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-  if (c < H) {
-    // Eight rows' loads in flight, added in token order.
-    constexpr int U = 8;
-    for (int t = t0; t < t1; t += U) {
-      float4 v[U];
-#pragma unroll
-      for (int u = 0; u < U; u++)
-        if (t + u < t1) v[u] = __ldcs(reinterpret_cast<const float4*>(h + (long)(t + u) * H + c));
-#pragma unroll
-      for (int u = 0; u < U; u++)
-        if (t + u < t1) {
-          acc.x += v[u].x;
-          acc.y += v[u].y;
-          acc.z += v[u].z;
-          acc.w += v[u].w;
-        }
-    }
-    if (t1 > t0) {
-      const float inv = __fdiv_rn(1.0f, (float)(t1 - t0));
-      acc.x = __fmul_rn(acc.x, inv);
-      acc.y = __fmul_rn(acc.y, inv);
-      acc.z = __fmul_rn(acc.z, inv);
-      acc.w = __fmul_rn(acc.w, inv);
-    }
-  }
-  float v[4] = {acc.x, acc.y, acc.z, acc.w};
-  for (int pass = 0; pass < 2; pass++) {
-    const int lim = pass == 0 ? H : out_dim;
-    if (pass == 1 && out_dim >= H) break;
-    double sq = 0.0;
-    for (int i = 0; i < 4; i++)
-      if (c + i < lim) sq += (double)v[i] * (double)v[i];
-    sq = warp_sum_d(sq);
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = (blockDim.x + 31) >> 5;
-    __syncthreads();
-    if (lane == 0) red[warp] = sq;
-    __syncthreads();
-    double tot = 0.0;
-    for (int i = 0; i < nw; i++) tot += red[i];
-    const double norm = sqrt(tot);
-    if (norm != 0.0) {
-      const float inv = (float)(1.0 / norm);
-      for (int i = 0; i < 4; i++) v[i] = __fmul_rn(v[i], inv);
-    }
-  }
-  for (int i = 0; i < 4; i++)
-    if (c + i < out_dim) out[(long)s * out_dim + c + i] = v[i];
+  pool_seq(h, offsets[s], offsets[s + 1], H, out_dim, out + (long)s * out_dim, red, [] { __syncthreads(); });
 }
 
 __global__ void f32_to_f16_kernel(const float* __restrict__ in, long n, __half* __restrict__ out) {

@@ -15,11 +15,16 @@
 //   ATT     (12 CTAs, one per head) once the head's 12 QKV tiles are done:
 //           attention of every sequence for that head
 //   OUT     (48 CTAs) once all heads are done: an output-projection tile
+//           (one sequence of at most 8 tokens: no ATT step; each OUT CTA
+//           computes every head's attention into shared memory itself once
+//           all QKV tiles are done)
 //   UG      every CTA, once all output tiles are done: LayerNorm, then its
 //           2-3 up/gate tiles with GEGLU
 //   DOWN    (144 CTAs) once every CTA finished UG: one K slice of a
 //           down-projection tile (48 tiles x 3 slices of 1,024 columns); the
 //           slices' partial sums are added by the LayerNorm that reads them
+// and at the end CTA s (s < number of sequences) applies the final LayerNorm
+// and mean-pools, normalises and truncates sequence s into the output.
 // Each hand-off is a release-add on a counter after the producing tile's
 // stores and an acquire poll by the consumers (bounded: WAIT_LIMIT_NS, then
 // DE_TIMEOUT and every CTA leaves); there is no grid-wide barrier.
@@ -33,6 +38,7 @@
 #include "gguf_decode.cuh"
 #include "kernels.h"
 #include "ln_warp.cuh"
+#include "pool_seq.cuh"
 #include "tcgen05.cuh"
 
 #include <mutex>
@@ -719,14 +725,19 @@ __global__ void __launch_bounds__(NTHREADS, 1) forward_small_kernel(const __grid
       }
     }
   }
-  // Final residual LayerNorm; one CTA writes h for the pooling kernel.
-  if (blockIdx.x == 0) {
+  // Final residual LayerNorm, then CTA s pools sequence s straight from its
+  // shared-memory rows (the pool kernel's thread layout and summation order).
+  if (blockIdx.x < p.nseq) {
     const SmallGemm& last = p.layers[p.n_layers - 1].g[3];
     if (!wait_cnt(p, S, CNT_Y2, (unsigned)(items_of(last) * p.n_layers), 75)) goto out;
     ln_rows(S.h, S.x, p.y2, p.layers[p.n_layers - 1].out_w, p.layers[p.n_layers - 1].out_b, p.eps, T,
             r16::n_slices(last.K));
     bar_compute();
-    for (int i = threadIdx.x; i < T * H; i += NCT) p.h_out[i] = S.h[i];
+    if (threadIdx.x < H / 4) {
+      const int s = blockIdx.x;
+      pool_seq(S.h, p.offsets[s], p.offsets[s + 1], H, p.out_dim, p.out + (long)s * p.out_dim,
+               reinterpret_cast<double*>(S.red), [] { asm volatile("bar.sync 2, %0;" ::"n"(H / 4) : "memory"); });
+    }
   }
 out:
   if (threadIdx.x == ISSUER) drain(S, pi);
@@ -736,7 +747,8 @@ out:
 
 bool small_forward_supported(const SmallParams& p, int hidden, int ffn, int heads, int sms) {
   if (hidden != SMALL_HIDDEN || ffn != SMALL_FFN || heads != SMALL_HEADS || p.T < 1 || p.T > SMALL_MAX_TOKENS ||
-      p.n_layers < 1 || p.n_layers > SMALL_MAX_LAYERS || sms < fs::HEADS)
+      p.n_layers < 1 || p.n_layers > SMALL_MAX_LAYERS || sms < fs::HEADS || p.nseq < 1 || p.nseq > sms ||
+      p.out_dim < 1 || p.out_dim > hidden)
     return false;
   for (int l = 0; l < p.n_layers; l++)
     for (int m = 0; m < 4; m++) {

@@ -91,7 +91,8 @@ struct SmallParams {
   float* y1;      // [T][H] attention-output projection
   __half* ff;     // [T][F]
   float* y2;      // [T][H] down projection
-  float* h_out;   // [T][H] final hidden states
+  float* out;     // [nseq][out_dim] pooled, normalised embeddings
+  int out_dim;
   unsigned* sync; // small_sync_bytes() of hand-off counters, zeroed by the launch
   DevStatus* status;
   SmallLayer layers[SMALL_MAX_LAYERS];
