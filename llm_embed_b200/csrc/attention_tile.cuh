@@ -166,9 +166,58 @@ __device__ __forceinline__ void attn_pv(const AttnRows& r, __half (*sK)[LDS], __
   store_rows(out, ldo, L, qrow0 + ((threadIdx.x & 31) >> 2), acc, l0, l1);
 }
 
+// Both passes for at most 16 keys (one 16-key chunk): the chunk's scores
+// are computed once and kept for the second pass; every operation and its
+// order are those of attn_max + attn_pv, so the bits are the same.
+__device__ __forceinline__ void attn_rows16_short(__half (*sQ)[LDS], int qrow_local, __half (*sK)[LDS],
+                                                  __half (*sV)[LDS], int L, __half* out, long ldo, int qrow0) {
+  AttnRows r;
+  load_q_frags(r.qa, sQ, qrow_local);
+  float s[2][4];
+  attn_scores(s[0], r, sK, 0, L);
+  attn_scores(s[1], r, sK, 1, L);
+  float mx0 = -INFINITY, mx1 = -INFINITY;
+#pragma unroll
+  for (int h = 0; h < 2; h++) {
+    mx0 = fmaxf(mx0, fmaxf(s[h][0], s[h][1]));
+    mx1 = fmaxf(mx1, fmaxf(s[h][2], s[h][3]));
+  }
+#pragma unroll
+  for (int o = 1; o <= 2; o <<= 1) {
+    mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, o));
+    mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, o));
+  }
+  float l0 = 0.f, l1 = 0.f;
+  float acc[8][4];
+#pragma unroll
+  for (int i = 0; i < 8; i++) acc[i][0] = acc[i][1] = acc[i][2] = acc[i][3] = 0.f;
+#pragma unroll
+  for (int h = 0; h < 2; h++) {
+    s[h][0] = ref_exp(__fsub_rn(s[h][0], mx0));
+    s[h][1] = ref_exp(__fsub_rn(s[h][1], mx0));
+    s[h][2] = ref_exp(__fsub_rn(s[h][2], mx1));
+    s[h][3] = ref_exp(__fsub_rn(s[h][3], mx1));
+    l0 += s[h][0] + s[h][1];
+    l1 += s[h][2] + s[h][3];
+  }
+  const uint32_t pa[4] = {pack_half2(s[0][0], s[0][1]), pack_half2(s[0][2], s[0][3]), pack_half2(s[1][0], s[1][1]),
+                          pack_half2(s[1][2], s[1][3])};
+  pv_chunk(acc, pa, sV, 0);
+#pragma unroll
+  for (int o = 1; o <= 2; o <<= 1) {
+    l0 += __shfl_xor_sync(0xffffffffu, l0, o);
+    l1 += __shfl_xor_sync(0xffffffffu, l1, o);
+  }
+  store_rows(out, ldo, L, qrow0 + ((threadIdx.x & 31) >> 2), acc, l0, l1);
+}
+
 // Both passes, for callers that have K and V in shared memory already.
 __device__ __forceinline__ void attn_rows16(__half (*sQ)[LDS], int qrow_local, __half (*sK)[LDS], __half (*sV)[LDS],
                                             int L, __half* out, long ldo, int qrow0) {
+  if (L <= 16) {
+    attn_rows16_short(sQ, qrow_local, sK, sV, L, out, ldo, qrow0);
+    return;
+  }
   AttnRows r;
   attn_max(r, sQ, qrow_local, sK, L);
   attn_pv(r, sK, sV, L, out, ldo, qrow0);
