@@ -110,14 +110,15 @@ __global__ void __launch_bounds__(256) ln_rows_kernel(const float* in, const flo
 }
 
 // pool.go:8-53 + embedder.go:59-68 (pool_seq.cuh): one CTA of H/4 threads
-// per sequence.
+// per sequence, 32 rows' loads in flight per thread (a 128-token sequence
+// is four DRAM round trips).
 __global__ void pool_kernel(const float* __restrict__ h, const int32_t* __restrict__ offsets, int H, int out_dim,
                             float* __restrict__ out) {
   pdl_wait();
   pdl_trigger();
   const int s = blockIdx.x;
   __shared__ double red[32];
-  pool_seq(h, offsets[s], offsets[s + 1], H, out_dim, out + (long)s * out_dim, red, [] { __syncthreads(); });
+  pool_seq<32>(h, offsets[s], offsets[s + 1], H, out_dim, out + (long)s * out_dim, red, [] { __syncthreads(); });
 }
 
 __global__ void f32_to_f16_kernel(const float* __restrict__ in, long n, __half* __restrict__ out) {

@@ -735,7 +735,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) forward_small_kernel(const __grid
     bar_compute();
     if (threadIdx.x < H / 4) {
       const int s = blockIdx.x;
-      pool_seq(S.h, p.offsets[s], p.offsets[s + 1], H, p.out_dim, p.out + (long)s * p.out_dim,
+      pool_seq<8>(S.h, p.offsets[s], p.offsets[s + 1], H, p.out_dim, p.out + (long)s * p.out_dim,
                reinterpret_cast<double*>(S.red), [] { asm volatile("bar.sync 2, %0;" ::"n"(H / 4) : "memory"); });
     }
   }

@@ -19,15 +19,14 @@ __device__ __forceinline__ double pool_warp_sum_d(double v) {
 // float32 multiply by float32(1/norm)), then truncation to out_dim and
 // renormalisation.  Called by threads 0 .. H/4-1 (whole warps), thread i
 // owning columns 4i..4i+3; `sync` is their barrier, `red` 32 doubles of
-// shared memory.  An empty sequence gives a zero vector.
-template <class Sync>
+// shared memory.  U rows' loads are in flight at once (their sum is still
+// formed in token order).  An empty sequence gives a zero vector.
+template <int U, class Sync>
 __device__ __forceinline__ void pool_seq(const float* h, int t0, int t1, int H, int out_dim, float* out_row,
                                          double* red, Sync sync) {
   const int c = threadIdx.x * 4;
   float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
   if (c < H) {
-    // Eight rows' loads in flight, added in token order.
-    constexpr int U = 8;
     for (int t = t0; t < t1; t += U) {
       float4 v[U];
 #pragma unroll
