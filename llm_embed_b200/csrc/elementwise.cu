@@ -73,10 +73,8 @@ __global__ void __launch_bounds__(256) ln_rows_kernel(const float* in, const flo
       if (i < nv) {
         const int c = (i * 32 + lane) * 4;
         const float4 t = *reinterpret_cast<const float4*>(type0 + c);
-        x[i].x = __fadd_rn(gguf_elem(emb_type, row, c + 0), t.x);
-        x[i].y = __fadd_rn(gguf_elem(emb_type, row, c + 1), t.y);
-        x[i].z = __fadd_rn(gguf_elem(emb_type, row, c + 2), t.z);
-        x[i].w = __fadd_rn(gguf_elem(emb_type, row, c + 3), t.w);
+        const float4 g = gguf_elem4(emb_type, row, c);
+        x[i] = make_float4(__fadd_rn(g.x, t.x), __fadd_rn(g.y, t.y), __fadd_rn(g.z, t.z), __fadd_rn(g.w, t.w));
       }
     }
   } else {
