@@ -25,12 +25,12 @@
 // next unit from a shared counter (unit u = descriptor u / heads, head u %
 // heads; CTA c takes c, c + grid, ... in turn) and issues everything
 // asynchronous of the group: the TMA loads of the next unit's Q|K (as soon
-// as S has read the current ones) and V (once the group has staged its
-// output through the V buffer), S of the next unit (once the group has read
-// O out of the slot), and P.V.  The four warps meet at two named barriers
-// per unit (P written; O read), and the elected thread's warp waits for the
-// others at a third (V buffer free).  No group ever waits for another, so a
-// long unit holds back only its own group.
+// as S has read the current ones), S of the next unit and its V (once the
+// group has read O out of the slot, P.V having read V), and P.V.  The four
+// warps meet at two named barriers per unit (P written; O read), then store
+// their rows' outputs straight from registers as whole 32-byte sectors.  No
+// group ever waits for another, so a long unit holds back only its own
+// group.
 //
 // Operands: one TMA map over qkv [T][3H] (64-column boxes of 64 rows,
 // 128-byte swizzle); Q and K K-major; V [keys][64] the MN-major B operand of
@@ -478,51 +478,39 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     if (group_any(bar_id, bad)) break;  // O is read: the slot is free
     cur = unit_next[(k + 1) & 1];
     if (elect && unit_la(cur) > 0) {
-      // S of the next unit, overlapping this unit's stores.
+      // S of the next unit, overlapping this unit's stores, and its V (P.V
+      // has read the V buffer: o_full).
       tc_fence_after();
       bad = !mbar_wait_sleep(qk_full, (k + 1) & 1, abort_flag, status, 81);
       if (!bad) gs.nqw++, issue_s(unit_np(cur)), gs.ns++;
+      if (!bad) load_v(cur), gs.nv++;
     }
     if (live && !bad) {
-      // O / l as fp16 through shared memory (the V buffer: P.V has read
-      // it), so that the global stores are whole 128-byte row segments:
-      // the warp writes its 32 rows (16-byte chunks swizzled by row) and
-      // reads them back four rows per instruction.  Rows past the sequence
-      // (l may be 0 there) are staged but never stored.
-      uint8_t* stg = smem + grp * Lay::GSTRIDE + 2 * QKV_BYTES + quarter * 32 * 128;
-      const float inv = 1.0f / l;
-      const unsigned long long inv2 = f2_pack(inv, inv);
+      // O / l as fp16, straight from registers: each row's 128 bytes as
+      // four 32-byte stores (whole sectors).  Rows past the sequence (l may
+      // be 0 there) are not stored.
+      const int rr = row - rbase;  // the row in its sequence
+      if (rr < L) {
+        const float inv = 1.0f / l;
+        const unsigned long long inv2 = f2_pack(inv, inv);
+        uint32_t* dst = reinterpret_cast<uint32_t*>(out + (long)(t0 + rr) * H + head * HD);
 #pragma unroll
-      for (int c = 0; c < 8; c++) {
-        uint32_t h[4];
+        for (int c = 0; c < 4; c++) {
+          uint32_t h[8];
 #pragma unroll
-        for (int j = 0; j < 4; j++) {
-          float a, b;
-          f2_unpack(f2_mul(f2_pack(__uint_as_float(o[8 * c + 2 * j]), __uint_as_float(o[8 * c + 2 * j + 1])), inv2), a,
-                    b);
-          h[j] = pack_half2(a, b);
+          for (int j = 0; j < 8; j++) {
+            float a, b;
+            f2_unpack(f2_mul(f2_pack(__uint_as_float(o[16 * c + 2 * j]), __uint_as_float(o[16 * c + 2 * j + 1])),
+                             inv2),
+                      a, b);
+            h[j] = pack_half2(a, b);
+          }
+          asm volatile("st.global.v8.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8};" ::"l"(dst + 8 * c), "r"(h[0]),
+                       "r"(h[1]), "r"(h[2]), "r"(h[3]), "r"(h[4]), "r"(h[5]), "r"(h[6]), "r"(h[7])
+                       : "memory");
         }
-        *reinterpret_cast<uint4*>(stg + lane * 128 + ((c ^ (lane & 7)) << 4)) = make_uint4(h[0], h[1], h[2], h[3]);
-      }
-      __syncwarp();
-      const int c = lane & 7;
-#pragma unroll
-      for (int i = 0; i < 8; i++) {
-        const int r = 4 * i + (lane >> 3);        // the warp's row
-        const int rr = quarter * 32 + r - rbase;  // the row in its sequence
-        const uint4 v = *reinterpret_cast<const uint4*>(stg + r * 128 + ((c ^ (r & 7)) << 4));
-        if (rr < L) reinterpret_cast<uint4*>(out + (long)(t0 + rr) * H + head * HD)[c] = v;
       }
     }
-    // The V buffer is free once every warp has read its rows back: the
-    // elected thread's warp waits for the others at a named barrier, then
-    // the next unit's V goes to the buffer.
-    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-    if (quarter == 0)
-      asm volatile("bar.sync %0, 128;" ::"r"(bar_id + G) : "memory");
-    else
-      asm volatile("bar.arrive %0, 128;" ::"r"(bar_id + G) : "memory");
-    if (elect && !bad && unit_la(gs.un) > 0) load_v(gs.un), gs.nv++;
   }
   // Copies and MMAs this group's elected thread issued but nobody waited
   // for (only after a failure) land before the CTA exits.
